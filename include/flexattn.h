@@ -1,0 +1,212 @@
+/*
+ * flexattn.h — C ABI of libflexattn.so, the B200 (sm_100a) FlexAttention engine.
+ *
+ * Every entry point is extern "C", takes plain pointers/sizes and a CUDA stream,
+ * returns an int status (FA_OK == 0) and never throws.  fa_last_error() returns a
+ * thread-local message for the last failure on the calling thread.  All buffers
+ * are owned by the caller; the library allocates no device memory on the hot path
+ * (the backward pass takes a caller-provided workspace sized by
+ * fa_bwd_workspace_size).
+ *
+ * Reference interface each entry point replaces (novastar53/pallas-flexattn,
+ * paths inside that project):
+ *   fa_fwd               <- flash_attention_fwd         src/pallas_flexattn/flash_attn.py:111-165
+ *                           (kernel body flash_attention_fwd_kernel, flash_attn.py:59-108)
+ *   fa_bwd               <- flash_attention_bwd         src/pallas_flexattn/flash_attn.py:410-461
+ *                           (preprocess :168-203, dK/dV :206-310, dQ :313-407)
+ *   fa_bwd_preprocess    <- flash_attention_bwd_preprocess flash_attn.py:176-203
+ *   fa_create_block_mask <- create_block_mask           src/pallas_flexattn/block_mask.py:54-129
+ *   fa_block_tables_from_lists <- BlockMask fields      src/pallas_flexattn/block_mask.py:16-51
+ *   fa_lse_merge         <- (no counterpart; combine step of the context-parallel ring)
+ */
+#ifndef FLEXATTN_H_
+#define FLEXATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* fa_stream_t; /* identical to cudaStream_t */
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum {
+  FA_OK = 0,
+  FA_ERR_INVALID = 1,     /* bad argument (shape, stride, pointer, dtype) */
+  FA_ERR_UNSUPPORTED = 2, /* valid request this build has no kernel for */
+  FA_ERR_CUDA = 3,        /* CUDA runtime/driver error */
+  FA_ERR_TIMEOUT = 4,     /* a device-side bounded wait gave up */
+};
+
+enum { FA_DTYPE_F32 = 0, FA_DTYPE_BF16 = 1 };
+
+/* Which kernel family runs the attention tiles. */
+enum {
+  FA_KERNEL_AUTO = 0, /* tcgen05 when the shape allows it, else the SIMT kernel */
+  FA_KERNEL_TC = 1,   /* sm_100a tcgen05/TMA/TMEM kernel; error if not applicable */
+  FA_KERNEL_SIMT = 2, /* generic CUDA-core kernel (fp32, any D <= 256, any block size) */
+};
+
+/* ------------------------------------------------------------------ mask_mod registry
+ * A mask is the AND of the enabled predicates on (q_idx, kv_idx):
+ *   CAUSAL      q >= kv                                   (mask_mod.py:15-17)
+ *   WINDOW      d = q - kv; (left < 0 || d <= left) && (right < 0 || -d <= right)
+ *                                                         (mask_mod.py:25-43)
+ *   DOCUMENT    doc_q[b][q] == doc_kv[b][kv]              (mask_mod.py:46-59 stub, built here)
+ *   TILE_TABLE  table[q / table_block][kv / table_block] != 0
+ * No flag set = bidirectional (mask_mod.py:20-22).  Elements with kv >= Tkv are
+ * always masked. */
+enum { FA_MASK_CAUSAL = 1, FA_MASK_WINDOW = 2, FA_MASK_DOCUMENT = 4, FA_MASK_TILE_TABLE = 8 };
+
+typedef struct {
+  int32_t flags;
+  int32_t window_left, window_right; /* -1 = unlimited */
+  const int32_t* doc_q;              /* [doc_b, Tq] device int32 document ids */
+  const int32_t* doc_kv;             /* [doc_b, Tkv] */
+  int64_t doc_stride_b;              /* elements between batches; 0 = shared by all batches */
+  const uint8_t* tile_table;         /* [table_rows, table_cols] device bytes, nonzero = keep */
+  int32_t table_rows, table_cols, table_block;
+} FaMaskSpec;
+
+/* ------------------------------------------------------------------ score_mod registry
+ * Applied in this order to the scaled logit s = scale * q.k:
+ *   ALIBI     s += slope[h] * (kv - q)
+ *   REL_BIAS  s += bias[h][q - kv + Tkv - 1]
+ *   SOFTCAP   s  = cap * tanh(s / cap)   (backward multiplies by 1 - tanh^2) */
+enum { FA_SCORE_ALIBI = 1, FA_SCORE_SOFTCAP = 2, FA_SCORE_REL_BIAS = 4 };
+
+typedef struct {
+  int32_t flags;
+  float softcap;
+  const float* alibi_slopes; /* [H] device fp32 */
+  const float* rel_bias;     /* [H or 1, Tq + Tkv - 1] device fp32 */
+  int64_t rel_bias_stride_h; /* 0 = one table for all heads */
+} FaScoreSpec;
+
+/* ------------------------------------------------------------------ block tables
+ * FlexAttention-style sparse tile tables.  For q block i, the kv blocks to visit
+ * with the mask applied are kv_indices[i][0 .. kv_num_blocks[i]) ("partial"), and
+ * the ones visited without evaluating the mask are full_kv_indices[i][0 ..
+ * full_kv_num_blocks[i]) ("full").  Blocks in neither list are skipped.  The q_*
+ * tables are the transpose (per kv block), used by the backward pass.  Tables
+ * carry a leading [num_b, num_h] index; a dimension of 1 broadcasts. */
+typedef struct {
+  int32_t block_q, block_kv; /* tile sizes the tables describe */
+  int32_t nq, nkv;           /* ceil(Tq / block_q), ceil(Tkv / block_kv) */
+  int32_t num_b, num_h;      /* 1 or B, 1 or H */
+  const int32_t* kv_num_blocks;      /* [num_b, num_h, nq] */
+  const int32_t* kv_indices;         /* [num_b, num_h, nq, kv_cap] */
+  const int32_t* full_kv_num_blocks; /* may be NULL */
+  const int32_t* full_kv_indices;
+  int32_t kv_cap;
+  const int32_t* q_num_blocks;      /* [num_b, num_h, nkv]; required by fa_bwd */
+  const int32_t* q_indices;         /* [num_b, num_h, nkv, q_cap] */
+  const int32_t* full_q_num_blocks; /* may be NULL */
+  const int32_t* full_q_indices;
+  int32_t q_cap;
+} FaBlockTables;
+
+/* A [B, H, T, D] tensor whose last dimension is contiguous. Strides in elements. */
+typedef struct {
+  void* ptr;
+  int64_t stride_b, stride_h, stride_t;
+} FaTensor;
+
+typedef struct {
+  int32_t dtype;            /* FA_DTYPE_BF16 or FA_DTYPE_F32; q/k/v/o share it */
+  int32_t B, H, H_kv;       /* H_kv divides H (grouped-query attention when < H) */
+  int32_t Tq, Tkv, D;
+  FaTensor q, k, v, o;
+  float* lse;               /* [B, H, Tq] fp32 natural-log logsumexp; contiguous */
+  float scale;              /* softmax scale (1/sqrt(D) in the reference) */
+  FaMaskSpec mask;
+  FaScoreSpec score;
+  FaBlockTables blocks;
+  int32_t kernel;           /* FA_KERNEL_* */
+  int32_t num_stages;       /* K/V pipeline depth for the tcgen05 kernel, 0 = default */
+  int32_t* status;          /* optional device int32: nonzero after a device-side timeout */
+} FaFwdParams;
+
+typedef struct {
+  int32_t dtype;
+  int32_t B, H, H_kv;       /* H_kv must equal H for the backward pass in this build */
+  int32_t Tq, Tkv, D;
+  FaTensor q, k, v, o, dout;
+  FaTensor dq, dk, dv;
+  const float* lse;         /* [B, H, Tq] from fa_fwd */
+  float scale;
+  FaMaskSpec mask;
+  FaScoreSpec score;
+  FaBlockTables blocks;
+  int32_t kernel;
+  int32_t num_stages;
+  int32_t* status;
+} FaBwdParams;
+
+/* ------------------------------------------------------------------ entry points */
+FA_API const char* fa_version(void);
+FA_API const char* fa_last_error(void);
+
+/* Forward: o, lse <- attention(q, k, v).  Rows with no unmasked key get o = 0 and
+ * lse = -inf. */
+FA_API int fa_fwd(const FaFwdParams* p, fa_stream_t stream);
+
+/* delta[b,h,t] = sum_d o*dout (fp32) and zero the fp32 dQ accumulator. */
+FA_API int fa_bwd_preprocess(const FaBwdParams* p, float* delta, float* dq_accum, fa_stream_t stream);
+
+/* Bytes of device workspace fa_bwd needs (delta + fp32 dQ accumulator). */
+FA_API int fa_bwd_workspace_size(const FaBwdParams* p, size_t* bytes);
+
+/* Backward: dq, dk, dv from (q, k, v, o, lse, dout).  Runs preprocess, the fused
+ * dK/dV/dQ kernel and the dQ conversion. */
+FA_API int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_stream_t stream);
+
+/* Block-mask construction on the GPU. */
+enum {
+  FA_BLOCK_MASK_EXACT = 0, /* tile listed iff any element is unmasked; "full" iff all are */
+  FA_BLOCK_MASK_REF9 = 1,  /* the reference's 3x3 sampling rule; every listed tile is partial */
+};
+
+typedef struct {
+  int32_t num_b, nq, nkv;        /* outputs are [num_b, 1, ...]; num_b = 1 unless the mask
+                                    depends on the batch (document ids with doc_stride_b != 0) */
+  uint8_t* tile_class;           /* [num_b, nq, nkv]: 0 skip, 1 partial, 2 full */
+  int32_t* kv_num_blocks;        /* [num_b, nq] */
+  int32_t* kv_indices;           /* [num_b, nq, nkv], rows padded with -1 */
+  int32_t* full_kv_num_blocks;   /* [num_b, nq] */
+  int32_t* full_kv_indices;      /* [num_b, nq, nkv] */
+  int32_t* q_num_blocks;         /* [num_b, nkv] */
+  int32_t* q_indices;            /* [num_b, nkv, nq] */
+  int32_t* full_q_num_blocks;    /* [num_b, nkv] */
+  int32_t* full_q_indices;       /* [num_b, nkv, nq] */
+} FaBlockMaskOut;
+
+FA_API int fa_create_block_mask(const FaMaskSpec* mask, int32_t B, int32_t Tq, int32_t Tkv, int32_t block_q,
+                         int32_t block_kv, int32_t mode, FaBlockMaskOut* out, fa_stream_t stream);
+
+/* Rebuild tile_class and all four table pairs of `out` from row lists (partial
+ * kv_num_blocks/kv_indices with row length kv_cap, optional full lists). */
+FA_API int fa_block_tables_from_lists(int32_t num_b, int32_t nq, int32_t nkv, const int32_t* kv_num_blocks,
+                               const int32_t* kv_indices, const int32_t* full_kv_num_blocks,
+                               const int32_t* full_kv_indices, int32_t kv_cap, FaBlockMaskOut* out,
+                               fa_stream_t stream);
+
+/* Combine two partial attention results over disjoint key sets, in place into
+ * (o_acc, lse_acc):  lse = logaddexp(lse_acc, lse_part);
+ *                    o   = o_acc*exp(lse_acc-lse) + o_part*exp(lse_part-lse).
+ * o_acc is fp32 [rows, D]; o_part is dtype [rows, D] with row stride o_part_stride. */
+FA_API int fa_lse_merge(int32_t rows, int32_t D, float* o_acc, float* lse_acc, const void* o_part,
+                 int64_t o_part_stride, int32_t o_part_dtype, const float* lse_part, fa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLEXATTN_H_ */

@@ -1,0 +1,451 @@
+// FlexAttention forward for B200 (sm_100a): TMA + tcgen05 + TMEM, warp-specialised.
+//
+// Replaces flash_attention_fwd / flash_attention_fwd_kernel of the reference
+// (src/pallas_flexattn/flash_attn.py:59-165).  Same math — online softmax over
+// KV tiles, O = softmax(mask(score(QK^T*scale))) V, per-row logsumexp — but:
+//   * each CTA owns two 128-row Q tiles of one (b, h) and walks the union of their
+//     block-table rows (kv_indices / full_kv_indices); empty tiles are skipped and
+//     full tiles do not evaluate the mask (the reference loops over every tile,
+//     flash_attn.py:101-104);
+//   * S = Q K^T and O += P V run on the 5th-gen tensor cores with the fp32
+//     accumulators in TMEM; P is written back to TMEM as bf16 (aliasing S) and fed
+//     to the PV MMA straight from TMEM;
+//   * the logsumexp is fp32 (the reference stores it in the input dtype,
+//     flash_attn.py:144).
+//
+// Warp roles (320 threads):
+//   warps 0-3  softmax for Q sub-tile 0 (thread = row)     warps 4-7  sub-tile 1
+//   warp 8     TMA producer (Q once, then K_j, V_j into an NS-slot ring)
+//   warp 9     MMA issuer (one thread) + TMEM owner
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
+// Per kv entry t the MMA thread issues PV_i(t) then S_i(t+1) for i = 0, 1, so one
+// sub-tile's softmax overlaps the other's tensor-core work.  Because tcgen05 ops of
+// one thread complete in issue order, the arrival of S_i(t+1) also proves PV_i(t)
+// is done, which is what lets the softmax warps rescale O without another barrier.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "fa_common.cuh"
+#include "fa_internal.h"
+#include "fa_ptx.cuh"
+
+namespace fa {
+
+namespace {
+
+constexpr int kBM = 128;          // rows of one Q sub-tile
+constexpr int kBN = 128;          // rows of one K/V tile
+constexpr int kFwdThreads = 320;  // 8 softmax warps + producer + MMA
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
+
+struct FwdSmemLayout {
+  int tile_bytes, q_off, kv_off, bar_off, misc_off, cls_off, ent_off, total;
+};
+
+__host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv) {
+  FwdSmemLayout L;
+  L.tile_bytes = kBM * D * 2;
+  L.q_off = 0;
+  L.kv_off = 2 * L.tile_bytes;
+  L.bar_off = L.kv_off + ns * L.tile_bytes;
+  L.misc_off = L.bar_off + (2 * ns + 8) * 8;
+  L.cls_off = L.misc_off + 16;
+  L.ent_off = L.cls_off + 4 * nkv;
+  L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
+  return L;
+}
+
+template <int D, int SK>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  constexpr int CHUNK_BYTES = kBM * 64 * 2;  // one 64-column, 128-byte-swizzled panel
+  constexpr int NCHUNK = D / 64;
+  constexpr uint32_t TM_S0 = 0, TM_O0 = 256;
+  constexpr uint32_t IDESC_S = make_idesc_bf16(kBM, kBN, 0, 0);
+  constexpr uint32_t IDESC_PV = make_idesc_bf16(kBM, D, 0, 1);
+
+  const int NS = a.num_stages;
+  const int nkv = a.bt.nkv;
+  const FwdSmemLayout L = fwd_smem_layout(D, NS, nkv);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L.q_off;
+  uint8_t* sKV = smem + L.kv_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* bar_q = bars;
+  uint64_t* bar_kv_full = bars + 1;
+  uint64_t* bar_kv_empty = bars + 1 + NS;
+  uint64_t* bar_s_full = bars + 1 + 2 * NS;   // [2]
+  uint64_t* bar_p_full = bar_s_full + 2;       // [2]
+  uint64_t* bar_o_full = bar_p_full + 2;       // [2]
+  uint64_t* bar_teardown = bar_o_full + 2;
+  int* misc = reinterpret_cast<int*>(smem + L.misc_off);
+  volatile int* abort_flag = misc;             // misc[0]
+  int* n_entries_s = misc + 1;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(misc + 2);
+  int* cls = reinterpret_cast<int*>(smem + L.cls_off);
+  int* entries = reinterpret_cast<int*>(smem + L.ent_off);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int BH = a.B * a.H;
+  const int npairs = (a.bt.nq + 1) >> 1;
+  const int bh = blockIdx.x % BH;
+  const int pair = npairs - 1 - (int)(blockIdx.x / BH);  // heaviest (last) q rows first
+  const int b = bh / a.H, h = bh % a.H;
+  const int hk = h / (a.H / a.Hkv);
+
+  // ---------------------------------------------------------------- setup
+  if (warp == 8 && lane == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar_kv_full + s, 1);
+      mbar_init(bar_kv_empty + s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_s_full + i, 1);
+      mbar_init(bar_p_full + i, 128);
+      mbar_init(bar_o_full + i, 1);
+    }
+    mbar_init(bar_teardown, 1);
+    misc[0] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_base_s, 512);
+    tmem_relinquish();
+  }
+  for (int j = tid; j < nkv; j += kFwdThreads) cls[j] = 0;
+  __syncthreads();
+
+  // Mark the kv tiles each sub-tile visits: bits 0-1 sub-tile 0, bits 2-3 sub-tile 1;
+  // code 1 = partial (mask applied), 2 = full.
+  {
+    const int64_t head = table_head(a.bt, b, h);
+    for (int i = 0; i < 2; ++i) {
+      const int qt = 2 * pair + i;
+      if (qt >= a.bt.nq) continue;
+      const int64_t row = head * a.bt.nq + qt;
+      const int np = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[row] : 0;
+      for (int e = tid; e < np; e += kFwdThreads) {
+        const int j = a.bt.kv_indices[row * a.bt.kv_cap + e];
+        if (j >= 0 && j < nkv) atomicOr(&cls[j], 1 << (2 * i));
+      }
+      const int nf = a.bt.full_kv_num_blocks ? a.bt.full_kv_num_blocks[row] : 0;
+      for (int e = tid; e < nf; e += kFwdThreads) {
+        const int j = a.bt.full_kv_indices[row * a.bt.kv_cap + e];
+        if (j >= 0 && j < nkv) atomicOr(&cls[j], 2 << (2 * i));
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 8) {
+    int base = 0;
+    for (int j0 = 0; j0 < nkv; j0 += 32) {
+      const int j = j0 + lane;
+      int c = (j < nkv) ? cls[j] : 0;
+      // A tile listed as both partial and full, or one that crosses Tkv, is treated as partial.
+      if ((c & 3) == 3) c = (c & ~3) | 1;
+      if ((c & 12) == 12) c = (c & ~12) | 4;
+      if ((j + 1) * kBN > a.Tkv) {
+        if ((c & 3) == 2) c = (c & ~3) | 1;
+        if ((c & 12) == 8) c = (c & ~12) | 4;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, c != 0);
+      if (c) entries[base + __popc(m & ((1u << lane) - 1u))] = j | (c << 24);
+      base += __popc(m);
+    }
+    if (lane == 0) *n_entries_s = base;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
+  const int n_ent = *n_entries_s;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && n_ent > 0) {
+      const bool has1 = (2 * pair + 1) < a.bt.nq;
+      mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
+      for (int i = 0; i < (has1 ? 2 : 1); ++i)
+        for (int c = 0; c < NCHUNK; ++c)
+          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (2 * pair + i) * kBM, h, b);
+      bool ok = true;
+      int issued = 0;  // loads issued so far (K and V alternate)
+      for (int t = 0; t < n_ent && ok; ++t) {
+        const int j = entries[t] & 0xFFFFFF;
+        for (int w = 0; w < 2 && ok; ++w, ++issued) {
+          const int slot = issued % NS, use = issued / NS;
+          if (!mbar_wait(bar_kv_empty + slot, (use & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar_kv_full + slot, L.tile_bytes);
+          for (int c = 0; c < NCHUNK; ++c)
+            tma_load_4d(sKV + slot * L.tile_bytes + c * CHUNK_BYTES, w ? &tm_v : &tm_k, bar_kv_full + slot, c * 64,
+                        j * kBN, hk, b);
+        }
+      }
+      if (!ok) {
+        report_status(a.status, FA_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // Teardown: make sure no bulk copy into this CTA's shared memory is still in flight.
+      volatile int never = 0;
+      mbar_wait(bar_q, 0, &never);
+      for (int s = 0; s < NS && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / NS) * NS;  // last load index that used slot s
+        mbar_wait(bar_kv_full + s, (last / NS) & 1, &never);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_ent > 0) {
+      const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
+      int last_t[2] = {-1, -1};
+      for (int t = 0; t < n_ent; ++t)
+        for (int i = 0; i < 2; ++i)
+          if ((entries[t] >> (24 + 2 * i)) & 3) last_t[i] = t;
+      bool ok = mbar_wait(bar_q, 0, abort_flag);
+      tc_fence_after();
+      uint32_t p_phase[2] = {0, 0};
+      int pv_count[2] = {0, 0};
+
+      auto issue_s = [&](int i, int t) -> bool {
+        const int slot = (2 * t) % NS;
+        if (!mbar_wait(bar_kv_full + slot, ((2 * t) / NS) & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t qa = sQa + i * L.tile_bytes, ka = sKVa + slot * L.tile_bytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+          mma_ss(tmem_base + TM_S0 + 128 * i, make_smem_desc(qa + off, 16, 1024, SMEM_SWIZZLE_128B),
+                 make_smem_desc(ka + off, 16, 1024, SMEM_SWIZZLE_128B), IDESC_S, kk > 0);
+        }
+        tc_commit(bar_s_full + i);
+        return true;
+      };
+      auto issue_pv = [&](int i, int t) -> bool {
+        const int slot = (2 * t + 1) % NS;
+        if (!mbar_wait(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar_p_full + i, p_phase[i], abort_flag)) return false;
+        p_phase[i] ^= 1;
+        tc_fence_after();
+        const uint32_t va = sKVa + slot * L.tile_bytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tmem_base + TM_O0 + D * i, tmem_base + TM_S0 + 128 * i + kk * 8,
+                 make_smem_desc(va + kk * 2048, CHUNK_BYTES, 1024, SMEM_SWIZZLE_128B), IDESC_PV,
+                 (pv_count[i] > 0 || kk > 0) ? 1u : 0u);
+        ++pv_count[i];
+        if (t == last_t[i]) tc_commit(bar_o_full + i);
+        return true;
+      };
+
+      if (ok) {
+        for (int i = 0; i < 2 && ok; ++i)
+          if ((entries[0] >> (24 + 2 * i)) & 3) ok = issue_s(i, 0);
+        if (ok) tc_commit(bar_kv_empty + 0);
+      }
+      for (int t = 0; t < n_ent && ok; ++t) {
+        const int e = entries[t];
+        const int en = (t + 1 < n_ent) ? entries[t + 1] : 0;
+        for (int i = 0; i < 2 && ok; ++i) {
+          if ((e >> (24 + 2 * i)) & 3) ok = issue_pv(i, t);
+          if (ok && t + 1 < n_ent && ((en >> (24 + 2 * i)) & 3)) ok = issue_s(i, t + 1);
+        }
+        if (!ok) break;
+        if (t + 1 < n_ent) tc_commit(bar_kv_empty + (2 * (t + 1)) % NS);
+        tc_commit(bar_kv_empty + (2 * t + 1) % NS);
+      }
+      if (!ok) {
+        report_status(a.status, FA_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // Teardown: wait (bounded) until every MMA issued above has retired.
+      tc_commit(bar_teardown);
+      volatile int never = 0;
+      mbar_wait(bar_teardown, 0, &never);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax (thread = row)
+    const int i = warp >> 2;
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const int q_row = (2 * pair + i) * kBM + r;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
+    const uint32_t tS = t_lane + TM_S0 + 128 * i;
+    const uint32_t tO = t_lane + TM_O0 + D * i;
+    const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
+    const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
+    const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && q_row < a.Tq ? __ldg(mc.doc_q + q_row) : 0;
+
+    float row_max = -INFINITY, row_sum = 0.f;
+    uint32_t s_phase = 0;
+    int processed = 0;
+    bool ok = true;
+    for (int t = 0; t < n_ent; ++t) {
+      const int e = entries[t];
+      const int code = (e >> (24 + 2 * i)) & 3;
+      if (!code) continue;
+      const int kv0 = (e & 0xFFFFFF) * kBN;
+      if (!mbar_wait(bar_s_full + i, s_phase, abort_flag)) { ok = false; break; }
+      s_phase ^= 1;
+      tc_fence_after();
+      float x[kBN];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(tS + 0, r0);
+        tmem_ld32(tS + 32, r1);
+        tmem_ld32(tS + 64, r2);
+        tmem_ld32(tS + 96, r3);
+        tmem_ld_wait();
+        reg_pin(r0); reg_pin(r1); reg_pin(r2); reg_pin(r3);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          x[c] = __uint_as_float(r0[c]);
+          x[32 + c] = __uint_as_float(r1[c]);
+          x[64 + c] = __uint_as_float(r2[c]);
+          x[96 + c] = __uint_as_float(r3[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], q_row, kv0 + c, sc);
+      if (code & 1) {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c)
+          if (!mask_ok(mc, q_row, kv0 + c, dq_val)) x[c] = -INFINITY;
+      }
+      float mloc = x[0];
+#pragma unroll
+      for (int c = 1; c < kBN; ++c) mloc = fmaxf(mloc, x[c]);
+      float alpha = 1.f;
+      const bool rescale = mloc > row_max + kRescaleThreshold;
+      if (rescale) {
+        alpha = ex2_approx(row_max - mloc);  // row_max = -inf gives 0
+        row_max = mloc;
+      }
+      const float m_use = (row_max == -INFINITY) ? 0.f : row_max;
+      float sum = 0.f;
+#pragma unroll
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float p0 = ex2_approx(x[c0 + c] - m_use);
+          const float p1 = ex2_approx(x[c0 + c + 1] - m_use);
+          sum += p0 + p1;
+          pk[c >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tS + (c0 >> 1), pk);
+      }
+      row_sum = row_sum * alpha + sum;
+      if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t ov[32];
+          tmem_ld32(tO + c0, ov);
+          tmem_ld_wait();
+          reg_pin(ov);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+          tmem_st32(tO + c0, ov);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar_p_full + i);
+      ++processed;
+    }
+    if (!ok) {
+      report_status(a.status, FA_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    bool have_o = ok && processed > 0;
+    if (have_o) {
+      have_o = mbar_wait(bar_o_full + i, 0, abort_flag);
+      if (!have_o) {
+        report_status(a.status, FA_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      tc_fence_after();
+    }
+    const bool live = row_sum > 0.f;
+    const float inv = live ? 1.f / row_sum : 0.f;
+    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
+                          (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t ov[32];
+      if (have_o) {
+        tmem_ld32(tO + c0, ov);
+        tmem_ld_wait();
+        reg_pin(ov);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) ov[c] = 0u;
+      }
+      if (q_row < a.Tq) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2)
+          pk[c >> 1] = pack_bf16x2(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
+        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+      }
+    }
+    if (q_row < a.Tq)
+      a.lse[(int64_t)bh * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace
+
+int fwd_tc_max_stages(int D, int nkv) {
+  int best = 0;
+  for (int ns = 2; ns <= 8; ++ns)
+    if (fwd_smem_layout(D, ns, nkv).total <= 227 * 1024) best = ns;
+  return best;
+}
+
+cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          cudaStream_t stream) {
+  const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv).total;
+  const int npairs = (a.bt.nq + 1) / 2;
+  const dim3 grid((unsigned)(npairs * a.B * a.H));
+  const int sk = score_kind_of(a.score.flags);
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a);
+    return cudaGetLastError();
+  };
+#define FA_FWD_CASE(DD, SKK) \
+  if (a.D == DD && sk == SKK) return go(fwd_tc_kernel<DD, SKK>);
+  FA_FWD_CASE(128, SC_NONE)
+  FA_FWD_CASE(128, SC_ALIBI)
+  FA_FWD_CASE(128, SC_SOFTCAP)
+  FA_FWD_CASE(128, SC_GENERAL)
+  FA_FWD_CASE(64, SC_NONE)
+  FA_FWD_CASE(64, SC_ALIBI)
+  FA_FWD_CASE(64, SC_SOFTCAP)
+  FA_FWD_CASE(64, SC_GENERAL)
+#undef FA_FWD_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fa
