@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""FlexAttention B200 benchmark: effective TFLOP/s of one forward+backward step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl flexattn|reference]
+
+A step is one forward and one backward pass (``flash_attention`` + autograd
+backward) of the chosen configuration (default cfg2: causal bf16
+B4 H16 S4096 D128) on inputs already resident in HBM.  Effective FLOPs count
+only unmasked (q, kv) pairs: forward 4*D*pairs*B*H, backward 2.5x that.
+
+Multi-GPU (torchrun): each rank runs its own B x H shard of the same size
+(weak scaling, no collective on the data path); time is the max over ranks.
+
+Extra keys: ``roofline`` for the dominant kernel (algorithmic FLOPs per launch
+over its CUDA-event duration, against the measured bf16 peak), ``cpu_baseline``
+(the reference's tiled CPU path restated in torch, on one (b, h) slice),
+``e2e`` (same step through the public API with pinned-host inputs copied in and
+a result row copied out each step), ``clocks`` (nvidia-smi sampled during the
+timed region) and ``gpu_launches``.
+
+``--impl reference`` times the reference's CPU implementation of the path (the
+restatement in oracle/cpu_reference.py; the reference itself needs jax, which
+is not installed) on this box's host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "pallas-flexattn_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+PEAK_FALLBACK = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+
+def load_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    d = dict(PEAK_FALLBACK)
+    d["source"] = "fallback"
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), world, local
+    return None, 0, 1, 0
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def max_over_ranks(dist, x: float, device) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(w, n_pairs: int, budget_s: float = 12.0) -> dict:
+    """Time the reference's tiled CPU path (torch restatement) on one (b, h) slice."""
+    from oracle import cpu_reference as ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(w.S, w.D, generator=g) * w.input_scale for _ in range(4))
+    flops = 3.5 * 4.0 * w.D * n_pairs  # fwd + bwd effective FLOPs of one slice
+    reps, t_tot = 0, 0.0
+    while t_tot < budget_s and reps < 50:
+        t0 = time.perf_counter()
+        o, lse = ref.fwd(q, k, v, w.mask_mod, w.score_mod)
+        ref.bwd(q, k, v, o, lse, do, w.mask_mod, w.score_mod)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    per = t_tot / reps
+    return {"value": flops / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x fwd+bwd of one (b,h) slice (S={w.S}, D={w.D}, fp32, all tiles as the reference); "
+                      f"{per * 1e3:.0f} ms per slice, x{w.B * w.H} slices = {per * w.B * w.H:.1f} s per full step"}
+
+
+def run_reference(args, w, n_pairs, rank):
+    if rank != 0:
+        return 0
+    from oracle import cpu_reference as ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(w.S, w.D, generator=g) * w.input_scale for _ in range(4))
+    flops = 3.5 * 4.0 * w.D * n_pairs
+
+    def step():
+        o, lse = ref.fwd(q, k, v, w.mask_mod, w.score_mod)
+        ref.bwd(q, k, v, o, lse, do, w.mask_mod, w.score_mod)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = flops / dt / 1e12
+    line = {
+        "impl": "reference", "metric": "effective TFLOP/s fwd+bwd (unmasked FLOPs)", "value": value,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D, "mask": w.desc,
+                   "sample": "one (b,h) slice per step"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"one (b,h) slice of {w.name} fwd+bwd per step, fp32, all tiles visited as "
+                                   "the reference's kernels do (oracle/cpu_reference.py)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU path restated in torch (the reference needs jax, which is not installed)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--impl", default="flexattn", choices=["flexattn", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from pallas_flexattn import workloads as W
+
+    w = W.get(args.config)
+    dist, rank, world, local = dist_setup()
+
+    if args.impl == "reference":
+        rc = run_reference(args, w, _pairs_cfg(w), rank)
+        if dist is not None:
+            dist.destroy_process_group()
+        return rc
+
+    import pallas_flexattn as pf
+    from pallas_flexattn import flash_attn as FA
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    n_pairs = W.count_pairs(w.mask_mod, w.S, w.S, device=device)
+    fwd_flops = w.fwd_flops(n_pairs)
+    bwd_flops = 2.5 * fwd_flops
+    q, k, v, do = w.inputs(device, seed=1000 + rank)
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        o = pf.flash_attention(q, k, v, w.mask_mod, score_mod=w.score_mod)
+        return torch.autograd.grad(o, (q, k, v), do)
+
+    def fwd_only():
+        return pf.flash_attention_fwd(q.detach(), k.detach(), v.detach(), w.mask_mod, score_mod=w.score_mod)
+
+    # warm-up (builds and caches block tables, loads kernels)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    FA.check_device_status(device)
+    plan = FA._Plan(q.detach(), k.detach(), v.detach(), w.mask_mod, w.score_mod, None, 64, 64, 3, None, True)
+    fwd_launches = 1
+    bwd_launches = 4  # preprocess + dQ kernel + dK/dV kernel + dQ convert (generic backward)
+
+    def timed(fn, n):
+        barrier(dist)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        barrier(dist)
+        return s.elapsed_time(e) / n
+
+    with ClockSampler(device.index) as clk:
+        ms_step = timed(step, args.steps)
+    ms_step = max_over_ranks(dist, ms_step, device)
+    ms_fwd = max_over_ranks(dist, timed(fwd_only, args.steps), device)
+    o0, lse0 = fwd_only()
+    o0 = o0.detach()
+
+    def bwd_only():
+        return FA.flash_attention_bwd(q.detach(), k.detach(), v.detach(), o0, lse0, do, w.mask_mod,
+                                      score_mod=w.score_mod)
+
+    ms_bwd = max_over_ranks(dist, timed(bwd_only, args.steps), device)
+    FA.check_device_status(device)
+
+    total_flops = (fwd_flops + bwd_flops) * world
+    value = total_flops / (ms_step * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    fwd_tf = fwd_flops / (ms_fwd * 1e-3) / 1e12
+    bwd_tf = bwd_flops / (ms_bwd * 1e-3) / 1e12
+    dominant = "bwd" if ms_bwd >= ms_fwd else "fwd"
+    ach = bwd_tf if dominant == "bwd" else fwd_tf
+    traffic = None
+    prof = REPO / "profiles" / "traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(f"{w.name}:{dominant}")
+
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (t.detach().to("cpu").pin_memory() for t in (q, k, v, do))
+        bq, bk, bv, bdo = (torch.empty_like(t.detach()) for t in (q, k, v, do))
+        out_host = torch.empty((w.B, w.H, w.D), dtype=q.dtype).pin_memory()
+
+        def e2e_step():
+            for dst, src in ((bq, hq), (bk, hk), (bv, hv), (bdo, hdo)):
+                dst.copy_(src, non_blocking=True)
+            qq, kk, vv = (t.requires_grad_(True) for t in (bq, bk, bv))
+            o = pf.flash_attention(qq, kk, vv, w.mask_mod, score_mod=w.score_mod)
+            torch.autograd.grad(o, (qq, kk, vv), bdo)
+            out_host.copy_(o[:, :, -1, :].detach(), non_blocking=True)
+            for t in (bq, bk, bv):
+                t.requires_grad_(False)
+
+        for _ in range(2):
+            e2e_step()
+        ms_e2e = max_over_ranks(dist, timed(e2e_step, max(3, args.steps // 2)), device)
+        e2e = {"value": total_flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": 4 * q.numel() * q.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(), "ms_per_step": ms_e2e}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, n_pairs)
+
+    if rank == 0:
+        line = {
+            "metric": "effective TFLOP/s fwd+bwd (unmasked FLOPs)", "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "S": w.S, "D": w.D, "mask": w.desc,
+                       "per_rank": f"B{w.B}xH{w.H} shard per GPU", "l2": "inputs larger than L2 (4x "
+                       f"{q.numel() * q.element_size() / 1e6:.0f} MB per rank)"},
+            "pct_of_peak": 100.0 * value / world / peak,
+            "fwd": {"ms": ms_fwd, "tflops": fwd_tf, "pct_of_peak": 100 * fwd_tf / peak,
+                    "pct_of_2250": 100 * fwd_tf / 2250.0, "kernel": "tcgen05" if plan.tc else "simt"},
+            "bwd": {"ms": ms_bwd, "tflops": bwd_tf, "pct_of_peak": 100 * bwd_tf / peak,
+                    "pct_of_2250": 100 * bwd_tf / 2250.0},
+            "roofline": {"bound": "tensor", "kernel": dominant, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                         "frac": ach / peak, "peak_source": f"bf16_tflops ({peaks['source']})",
+                         "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps * (fwd_launches + bwd_launches),
+            "unmasked_pairs_per_bh": n_pairs,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def _pairs_cfg(w) -> int:
+    from pallas_flexattn import workloads as W
+
+    if "tile_table" in w.extra:
+        import numpy as np
+
+        t = w.extra["tile_table"]
+        n = t.shape[0]
+        return int(np.tril(t, -1).sum()) * 128 * 128 + n * (128 * 129 // 2)
+    return W.count_pairs(w.mask_mod, w.S, w.S)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -161,7 +161,9 @@ class _Plan:
         if bt.num_b not in (1, B):
             raise ValueError("block mask batch dimension does not match B")
         self.tables = bt
-        self.kernel = L.FA_KERNEL_TC if tc else L.FA_KERNEL_SIMT
+        # AUTO lets the library take the tcgen05 kernel of each pass when it applies.
+        self.tc = tc
+        self.kernel = L.FA_KERNEL_AUTO if tc else L.FA_KERNEL_SIMT
         self.num_stages = int(num_stages) if num_stages else 0
         self.c_mask = mspec.to_c(self.device, Tq, Tkv)
         self.c_score = sspec.to_c(self.device, H, Tq, Tkv)

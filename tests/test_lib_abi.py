@@ -1,0 +1,68 @@
+"""The C ABI without a GPU: libflexattn.so loads, exports every entry point that
+include/flexattn.h declares, and the ctypes structures match the header's layout
+(sizes and field offsets printed by a gcc-compiled probe of the header)."""
+import ctypes as C
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from pallas_flexattn import _lib as L
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "flexattn.h"
+STRUCTS = ["FaMaskSpec", "FaScoreSpec", "FaBlockTables", "FaTensor", "FaFwdParams", "FaBwdParams", "FaBlockMaskOut"]
+
+
+def declared_functions():
+    return re.findall(r"FA_API\s+[\w\s\*]+?\b(fa_\w+)\s*\(", HEADER.read_text())
+
+
+def test_library_loads_and_reports_version():
+    assert L.version().startswith("flexattn-b200")
+
+
+def test_every_declared_entry_point_is_exported_and_bound():
+    names = declared_functions()
+    assert len(names) >= 9
+    lib = L.lib()
+    for n in names:
+        assert hasattr(lib, n), f"{n} not exported"
+        assert n in L.EXPORTS, f"{n} not bound in _lib.EXPORTS"
+    assert set(L.EXPORTS) == set(names)
+
+
+def test_error_path_without_gpu():
+    p = L.FaFwdParams()
+    rc = L.lib().fa_fwd(C.byref(p), None)
+    assert rc == L.FA_ERR_INVALID
+    assert b"shape" in L.lib().fa_last_error() or b"dtype" in L.lib().fa_last_error()
+    size = C.c_size_t(0)
+    bp = L.FaBwdParams()
+    bp.B, bp.H, bp.Tq, bp.D = 2, 3, 5, 64
+    assert L.lib().fa_bwd_workspace_size(C.byref(bp), C.byref(size)) == 0
+    assert size.value >= 2 * 3 * 5 * 4 + 2 * 3 * 5 * 64 * 4
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_ctypes_layout_matches_header(tmp_path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "flexattn.h"', "int main(void) {"]
+    for s in STRUCTS:
+        cls = getattr(L, s)
+        lines.append(f'printf("{s} size %zu\\n", sizeof({s}));')
+        for f, _ in cls._fields_:
+            lines.append(f'printf("{s}.{f} %zu\\n", offsetof({s}, {f}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", f"-I{REPO / 'include'}", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = dict(line.rsplit(" ", 1) for line in out if line)
+    for s in STRUCTS:
+        cls = getattr(L, s)
+        assert int(got[f"{s} size"]) == C.sizeof(cls), s
+        for f, _ in cls._fields_:
+            assert int(got[f"{s}.{f}"]) == getattr(cls, f).offset, f"{s}.{f}"
