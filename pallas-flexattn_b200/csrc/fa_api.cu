@@ -184,10 +184,14 @@ static int check_bwd(const FaBwdParams* p) {
 
 static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+static int pad128(int t) { return (t + 127) / 128 * 128; }
+
+// Workspace: delta [B*H, Tq_pad] | lse2 [B*H, Tq_pad] | dq_accum [B*H, Tq, D], fp32.
 int fa_bwd_workspace_size(const FaBwdParams* p, size_t* bytes) {
   if (!p || !bytes) return fail(FA_ERR_INVALID, "NULL argument");
+  const size_t prow = (size_t)p->B * p->H * pad128(p->Tq);
   const size_t rows = (size_t)p->B * p->H * p->Tq;
-  *bytes = round_up(rows * sizeof(float), 256) + round_up(rows * p->D * sizeof(float), 256);
+  *bytes = 2 * round_up(prow * sizeof(float), 256) + round_up(rows * p->D * sizeof(float), 256);
   return FA_OK;
 }
 
@@ -197,6 +201,8 @@ int fa_bwd_preprocess(const FaBwdParams* p, float* delta, float* dq_accum, fa_st
   if (!delta || !dq_accum) return fail(FA_ERR_INVALID, "delta / dq_accum is NULL");
   AttnArgs a = base_args(p->B, p->H, p->H_kv, p->Tq, p->Tkv, p->D, p->scale, p->mask, p->score, p->blocks, p->status);
   a.o = p->o; a.dout = p->dout; a.delta = delta; a.dq_accum = dq_accum;
+  a.Tq_pad = p->Tq;  // public form: delta is [B*H, Tq], no log2 logsumexp
+  a.lse2 = nullptr;
   cudaError_t e = launch_bwd_preprocess(a, p->dtype, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "fa_bwd_preprocess");
   return FA_OK;
@@ -210,14 +216,17 @@ int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_str
   if (!workspace || workspace_bytes < need)
     return fail(FA_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, need);
   if (!aligned16(workspace)) return fail(FA_ERR_INVALID, "workspace must be 16-byte aligned");
-  const size_t rows = (size_t)p->B * p->H * p->Tq;
-  float* delta = reinterpret_cast<float*>(workspace);
-  float* dq_accum = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + round_up(rows * 4, 256));
+  const size_t prow_bytes = round_up((size_t)p->B * p->H * pad128(p->Tq) * 4, 256);
+  char* ws = reinterpret_cast<char*>(workspace);
 
   AttnArgs a = base_args(p->B, p->H, p->H_kv, p->Tq, p->Tkv, p->D, p->scale, p->mask, p->score, p->blocks, p->status);
   a.q = p->q; a.k = p->k; a.v = p->v; a.o = p->o; a.dout = p->dout;
   a.dq = p->dq; a.dk = p->dk; a.dv = p->dv;
-  a.lse_in = p->lse; a.delta = delta; a.dq_accum = dq_accum;
+  a.lse_in = p->lse;
+  a.Tq_pad = pad128(p->Tq);
+  a.delta = reinterpret_cast<float*>(ws);
+  a.lse2 = reinterpret_cast<float*>(ws + prow_bytes);
+  a.dq_accum = reinterpret_cast<float*>(ws + 2 * prow_bytes);
 
   cudaError_t e = launch_bwd_preprocess(a, p->dtype, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "fa_bwd preprocess");

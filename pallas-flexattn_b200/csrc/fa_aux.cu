@@ -25,14 +25,25 @@ __device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
+// One warp per row of the padded [B*H, Tq_pad] grid.  Rows past Tq get delta = 0
+// and lse2 = +inf (so exp2(x - lse2) = 0 there); rows with lse = -inf (no key)
+// also get lse2 = +inf.
 template <typename T>
 __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const AttnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + warp;  // over B*H*Tq
-  const int64_t rows = (int64_t)a.B * a.H * a.Tq;
-  if (row >= rows) return;
-  const int t = (int)(row % a.Tq);
-  const int bh = (int)(row / a.Tq), b = bh / a.H, h = bh % a.H;
+  const int64_t prow = (int64_t)blockIdx.x * kRowsPerCta + warp;  // over B*H*Tq_pad
+  const int64_t prows = (int64_t)a.B * a.H * a.Tq_pad;
+  if (prow >= prows) return;
+  const int t = (int)(prow % a.Tq_pad);
+  const int bh = (int)(prow / a.Tq_pad), b = bh / a.H, h = bh % a.H;
+  if (t >= a.Tq) {
+    if (lane == 0) {
+      a.delta[prow] = 0.f;
+      if (a.lse2) a.lse2[prow] = INFINITY;
+    }
+    return;
+  }
+  const int64_t row = (int64_t)bh * a.Tq + t;
   const T* o = reinterpret_cast<const T*>(a.o.ptr) + (int64_t)b * a.o.stride_b + (int64_t)h * a.o.stride_h +
                (int64_t)t * a.o.stride_t;
   const T* g = reinterpret_cast<const T*>(a.dout.ptr) + (int64_t)b * a.dout.stride_b +
@@ -54,7 +65,13 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const Attn
   }
 #pragma unroll
   for (int s = 16; s; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-  if (lane == 0) a.delta[row] = acc;
+  if (lane == 0) {
+    a.delta[prow] = acc;
+    if (a.lse2) {
+      const float l = a.lse_in[row];
+      a.lse2[prow] = (l == -INFINITY) ? INFINITY : l * kLog2e;
+    }
+  }
   float4* z = reinterpret_cast<float4*>(a.dq_accum + row * a.D);
   for (int d4 = lane; d4 < a.D / 4; d4 += 32) z[d4] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
@@ -100,7 +117,7 @@ __global__ void __launch_bounds__(kRowsPerCta * 32)
 }  // namespace
 
 cudaError_t launch_bwd_preprocess(const AttnArgs& a, int dtype, cudaStream_t stream) {
-  const int64_t rows = (int64_t)a.B * a.H * a.Tq;
+  const int64_t rows = (int64_t)a.B * a.H * a.Tq_pad;
   const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
   if (dtype == FA_DTYPE_F32) preprocess_kernel<float><<<grid, kRowsPerCta * 32, 0, stream>>>(a);
   else preprocess_kernel<__nv_bfloat16><<<grid, kRowsPerCta * 32, 0, stream>>>(a);

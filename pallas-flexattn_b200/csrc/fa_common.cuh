@@ -139,9 +139,11 @@ struct AttnArgs {
   int B, H, Hkv, Tq, Tkv, D;
   FaTensor q, k, v, o, dout, dq, dk, dv;
   float* lse;
-  const float* lse_in;
-  float* delta;
-  float* dq_accum;
+  const float* lse_in;  // [B*H, Tq] natural-log logsumexp from the forward pass
+  int Tq_pad;           // Tq rounded up to 128: row length of lse2 and delta
+  float* lse2;          // [B*H, Tq_pad] lse * log2(e); +inf on padding and empty rows
+  float* delta;         // [B*H, Tq_pad] rowsum(O * dO); 0 on padding
+  float* dq_accum;      // [B*H, Tq, D] fp32 dQ accumulator (unscaled)
   float scale;
   FaMaskSpec mask;
   FaScoreSpec score;

@@ -283,6 +283,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
     const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && q_row < a.Tq ? __ldg(mc.doc_q + q_row) : 0;
+    // Causal, window and the Tkv bound intersect to one allowed kv interval [row_lo, row_hi]
+    // per row; partial tiles test it with two compares.  Document and tile-table predicates
+    // (if enabled) are evaluated per element on top.
+    int row_lo = 0, row_hi = a.Tkv - 1;
+    if (mc.flags & FA_MASK_CAUSAL) row_hi = min(row_hi, q_row);
+    if (mc.flags & FA_MASK_WINDOW) {
+      if (mc.left >= 0) row_lo = max(row_lo, q_row - mc.left);
+      if (mc.right >= 0) row_hi = min(row_hi, q_row + mc.right);
+    }
+    const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
 
     float row_max = -INFINITY, row_sum = 0.f;
     uint32_t s_phase = 0;
@@ -313,16 +323,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           x[96 + c] = __uint_as_float(r3[c]);
         }
       }
+      // Without a score_mod the mask and the max work on the raw dot products (the
+      // scale is positive) and the scale folds into the exponent's FFMA.
+      if constexpr (SK != SC_NONE) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], q_row, kv0 + c, sc);
+        for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], q_row, kv0 + c, sc);
+      }
       if (code & 1) {
+        const unsigned span = (unsigned)(row_hi - row_lo);
+        const int clo = row_lo - kv0;
 #pragma unroll
         for (int c = 0; c < kBN; ++c)
-          if (!mask_ok(mc, q_row, kv0 + c, dq_val)) x[c] = -INFINITY;
-      }
-      float mloc = x[0];
+          if ((unsigned)(c - clo) > span || row_hi < row_lo) x[c] = -INFINITY;
+        if (per_elem_mask) {
 #pragma unroll
-      for (int c = 1; c < kBN; ++c) mloc = fmaxf(mloc, x[c]);
+          for (int c = 0; c < kBN; ++c)
+            if (!mask_ok(mc, q_row, kv0 + c, dq_val)) x[c] = -INFINITY;
+        }
+      }
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = x[k];
+#pragma unroll
+      for (int c = 8; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
+      float mloc = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                         fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      if constexpr (SK == SC_NONE) mloc *= sc.k_log2;
       float alpha = 1.f;
       const bool rescale = mloc > row_max + kRescaleThreshold;
       if (rescale) {
@@ -330,19 +356,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         row_max = mloc;
       }
       const float m_use = (row_max == -INFINITY) ? 0.f : row_max;
-      float sum = 0.f;
+      const float2 kk2 = make_float2(SK == SC_NONE ? sc.k_log2 : 1.f, SK == SC_NONE ? sc.k_log2 : 1.f);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          const float p0 = ex2_approx(x[c0 + c] - m_use);
-          const float p1 = ex2_approx(x[c0 + c + 1] - m_use);
-          sum += p0 + p1;
-          pk[c >> 1] = pack_bf16x2(p0, p1);
+          const float2 y = __ffma2_rn(make_float2(x[c0 + c], x[c0 + c + 1]), kk2, nm2);
+          const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+          sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
+          pk[c >> 1] = pack_bf16x2(p.x, p.y);
         }
         tmem_st16(tS + (c0 >> 1), pk);
       }
+      const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+      const float2 s4 = __fadd2_rn(s01, s23);
+      const float sum = s4.x + s4.y;
       row_sum = row_sum * alpha + sum;
       if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1

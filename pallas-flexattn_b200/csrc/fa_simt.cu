@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dq_simt_kernel(const AttnArgs
       sdO[warp * D + d] = to_f(g[d]);
     }
     lse = a.lse_in[(int64_t)bh * a.Tq + q_row];
-    delta = a.delta[(int64_t)bh * a.Tq + q_row];
+    delta = a.delta[(int64_t)bh * a.Tq_pad + q_row];
   }
   const int64_t trow = table_head(a.bt, b, h) * a.bt.nq + qb;
   const RowList L = row_list(a.bt.kv_num_blocks, a.bt.kv_indices, a.bt.full_kv_num_blocks, a.bt.full_kv_indices, trow,
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dkv_simt_kernel(const AttnArg
       for (int r = threadIdx.x; r < kChunk; r += blockDim.x) {
         const int q = c0 + r;
         sL[r] = q < t_end ? a.lse_in[(int64_t)bh * a.Tq + q] : -INFINITY;
-        sDl[r] = q < t_end ? a.delta[(int64_t)bh * a.Tq + q] : 0.f;
+        sDl[r] = q < t_end ? a.delta[(int64_t)bh * a.Tq_pad + q] : 0.f;
         sDoc[r] = (q < t_end && (mc.flags & FA_MASK_DOCUMENT)) ? mc.doc_q[q] : 0;
       }
       __syncthreads();

@@ -1,0 +1,318 @@
+"""GPU parity: the CUDA kernels through the public API against the CPU oracle.
+
+Tolerance (the acceptance bar for bf16): relative-L2 <= 5e-3 and, element by
+element, |err| <= 2e-2 + 2^-8 |ref| against an fp32/fp64 reference on the same
+(bf16-rounded) inputs, for o and for dq/dk/dv.  The 2^-8 |ref| term is the
+rounding of a bf16 output itself (half a unit in the last place), which alone
+exceeds 2e-2 once |ref| > 5.  fp32 inputs (generic kernels) are held to 2e-4 /
+1e-5 with no relative term.  Small shapes
+use the numpy oracle (oracle/flexattn_oracle.py); full-length benchmark shapes
+use a chunked fp32 torch reference of the same formulas, itself checked against
+the oracle here.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import pallas_flexattn as pf
+from oracle import flexattn_oracle as O
+from pallas_flexattn import workloads as W
+from pallas_flexattn.flash_attn import check_device_status
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+TOL = {torch.bfloat16: (2e-2, 5e-3, 2.0 ** -8), torch.float32: (2e-4, 1e-5, 0.0)}
+
+
+def inputs(shape_q, shape_kv, dtype, seed=0, scale=1.0):
+    rng = np.random.default_rng(seed)
+    mk = lambda s: torch.from_numpy((rng.standard_normal(s) * scale).astype(np.float32)).to(DEV, dtype)  # noqa: E731
+    return mk(shape_q), mk(shape_kv), mk(shape_kv), mk(shape_q)
+
+
+def close(name, got, ref, dtype):
+    got = got.detach().float().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    ref = ref.detach().float().cpu().numpy() if isinstance(ref, torch.Tensor) else np.asarray(ref)
+    atol, rtol, elem_rel = TOL[dtype]
+    if not got.size:
+        return
+    diff = np.abs(got - ref)
+    err = float(diff.max())
+    excess = float((diff - (atol + elem_rel * np.abs(ref))).max())
+    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    assert excess <= 0 and rel <= rtol, (f"{name}: max-abs {err:.3e} (bound {atol} + {elem_rel:.2e}|ref|, "
+                                         f"worst excess {excess:.2e}), rel-L2 {rel:.3e} (<= {rtol})")
+
+
+def run_api(q, k, v, do, mask_mod=None, score_mod=None, block_mask=None, bwd=True, **kw):
+    q, k, v = (t.detach().clone().requires_grad_(bwd) for t in (q, k, v))
+    o = pf.flash_attention(q, k, v, mask_mod, score_mod=score_mod, block_mask=block_mask, **kw)
+    grads = torch.autograd.grad(o, (q, k, v), do) if bwd else None
+    torch.cuda.synchronize()
+    check_device_status(DEV)
+    return o, grads
+
+
+def oracle(q, k, v, do, mask=None, mods=()):
+    qf, kf, vf, dof = (t.detach().float().cpu().numpy().astype(np.float64) for t in (q, k, v, do))
+    o, lse = O.mha_reference(qf, kf, vf, mask, mods)
+    return o, lse, O.attention_bwd(qf, kf, vf, o, lse, dof, mask, mods)
+
+
+def check_all(q, k, v, do, mask_mod, omask, score_mod=None, omods=(), bwd=True, block_mask=None, **kw):
+    o, g = run_api(q, k, v, do, mask_mod, score_mod, block_mask=block_mask, bwd=bwd, **kw)
+    ro, rlse, rg = oracle(q, k, v, do, omask, omods)
+    close("o", o, ro, q.dtype)
+    if bwd:
+        for n, a, b in zip(("dq", "dk", "dv"), g, rg):
+            close(n, a, b, q.dtype)
+
+
+# ------------------------------------------------------------------------ the reference's test suite
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("mname", ["causal", "bidir", "window32"])
+def test_reference_forward_and_gradients(dtype, mname):
+    """tests/test_flash_attn.py:43-71,117-135 of the reference (B2 H4 T128 D64)."""
+    mm, om = {"causal": (pf.causal_mask, O.causal), "bidir": (pf.bidirectional_mask, O.bidirectional),
+              "window32": (pf.sliding_window_mask(32, 32), O.sliding_window(32, 32))}[mname]
+    q, k, v, do = inputs((2, 4, 128, 64), (2, 4, 128, 64), dtype)
+    check_all(q, k, v, do, mm, om)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B", [1, 2, 4])
+def test_batch_sizes(dtype, B):
+    q, k, v, do = inputs((B, 4, 64, 32), (B, 4, 64, 32), dtype, seed=B)
+    check_all(q, k, v, do, None, None)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128, 256])
+def test_head_dims(dtype, D):
+    q, k, v, do = inputs((2, 4, 64, D), (2, 4, 64, D), dtype, seed=D)
+    check_all(q, k, v, do, pf.causal_mask, O.causal)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_large_sequence_length(dtype):
+    q, k, v, do = inputs((1, 2, 512, 64), (1, 2, 512, 64), dtype, seed=7)
+    check_all(q, k, v, do, None, None)
+
+
+def test_no_nan_no_inf_and_shapes():
+    q, k, v, do = inputs((2, 4, 128, 64), (2, 4, 128, 64), torch.bfloat16)
+    o, (dq, dk, dv) = run_api(q, k, v, do)
+    assert o.shape == q.shape and dq.shape == q.shape and dk.shape == k.shape and dv.shape == v.shape
+    for t in (o, dq, dk, dv):
+        assert torch.isfinite(t).all()
+
+
+# ------------------------------------------------------------------------ golden: the reference's own kernels
+GOLD = np.load(__import__("pathlib").Path(__file__).resolve().parent / "golden" / "attention.npz")
+GMASK = {"causal_B1H2T128D32": pf.causal_mask, "bidir_B1H2T128D32": pf.bidirectional_mask,
+         "window32_B1H2T128D32": pf.sliding_window_mask(32, 32), "causal_B1H2T128D64": pf.causal_mask}
+
+
+@pytest.mark.parametrize("name", sorted(GMASK))
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_matches_reference_kernel_outputs(name, dtype):
+    g = {k: GOLD[f"{name}/{k}"] for k in ("q", "k", "v", "do", "o", "lse", "dq", "dk", "dv")}
+    q, k, v, do = (torch.from_numpy(g[n]).to(DEV, dtype) for n in ("q", "k", "v", "do"))
+    o, lse = pf.flash_attention_fwd(q, k, v, GMASK[name])
+    dq, dk, dv = pf.flash_attention_bwd(q, k, v, o, lse, do, GMASK[name])
+    torch.cuda.synchronize()
+    if dtype == torch.float32:
+        close("o", o, g["o"], dtype)
+        close("lse", lse, g["lse"], dtype)
+        for n, a in (("dq", dq), ("dk", dk), ("dv", dv)):
+            close(n, a, g[n], dtype)
+    else:  # bf16 inputs differ from the fp32 golden inputs: compare against the oracle on them
+        check_all(q, k, v, do, GMASK[name], None if "bidir" in name else {
+            "causal_B1H2T128D32": O.causal, "causal_B1H2T128D64": O.causal,
+            "window32_B1H2T128D32": O.sliding_window(32, 32)}[name])
+
+
+# ------------------------------------------------------------------------ score_mods
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("kind", ["alibi", "softcap", "relbias", "alibi+softcap"])
+def test_score_mods(D, kind):
+    H, T = 3, 384
+    q, k, v, do = inputs((1, H, T, D), (1, H, T, D), torch.bfloat16, seed=11)
+    slopes = O.alibi_slopes(H)
+    bias = np.random.default_rng(5).standard_normal((H, 2 * T - 1)).astype(np.float32) * 0.5
+    al, om_al = pf.alibi_score_mod(H), O.alibi(slopes)
+    sc, om_sc = pf.softcap_score_mod(2.5), O.softcap(2.5)
+    rb = pf.relative_bias_score_mod(bias)
+
+    def om_rb(s, h, qi, ki):
+        return s + bias.astype(np.float64)[h, qi - ki + T - 1]
+
+    om_rb.grad = None
+    sm, om = {"alibi": (al, (om_al,)), "softcap": (sc, (om_sc,)), "relbias": (rb, (om_rb,)),
+              "alibi+softcap": (pf.compose_score_mods(sc, al), (om_al, om_sc))}[kind]
+    check_all(q, k, v, do, pf.causal_mask, O.causal, sm, om)
+
+
+# ------------------------------------------------------------------------ masks and shapes
+@pytest.mark.parametrize("D", [64, 128])
+def test_document_and_tile_masks(D):
+    T = 640
+    lens = [100, 250, 37, 253]
+    doc = np.repeat(np.arange(4), lens)
+    q, k, v, do = inputs((1, 2, T, D), (1, 2, T, D), torch.bfloat16, seed=3)
+    check_all(q, k, v, do, pf.and_masks(pf.document_mask(lens), pf.causal_mask), O.and_(O.document(doc), O.causal))
+    table = W.random_tile_table(5, 0.4, seed=2)
+    check_all(q, k, v, do, pf.and_masks(pf.causal_mask, pf.tile_mask(table, 128)),
+              O.and_(O.causal, O.tile_table(table, 128)))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T", [1, 77, 200, 300, 129])
+def test_ragged_lengths(dtype, T):
+    q, k, v, do = inputs((1, 2, T, 64), (1, 2, T, 64), dtype, seed=T)
+    check_all(q, k, v, do, pf.causal_mask, O.causal)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_cross_attention_lengths(dtype):
+    q, k, v, do = inputs((2, 2, 256, 128), (2, 2, 384, 128), dtype, seed=9)
+    check_all(q, k, v, do, pf.causal_mask, O.causal)
+    q, k, v, do = inputs((1, 2, 300, 64), (1, 2, 130, 64), dtype, seed=10)
+    check_all(q, k, v, do, None, None)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_grouped_query_forward(D):
+    q, k, v, do = inputs((2, 8, 256, D), (2, 2, 256, D), torch.bfloat16, seed=12)
+    o, _ = run_api(q, k, v, do, pf.causal_mask, bwd=False)
+    kr, vr = k.repeat_interleave(4, dim=1), v.repeat_interleave(4, dim=1)
+    ro, _, _ = oracle(q, kr, vr, do, O.causal)
+    close("o", o, ro, torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        run_api(q, k, v, do, pf.causal_mask, bwd=True)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fully_masked_rows_give_zero_output_and_gradients(dtype):
+    table = np.array([[0, 0], [1, 1]], np.uint8)  # q block 0 sees nothing
+    q, k, v, do = inputs((1, 2, 256, 64), (1, 2, 256, 64), dtype, seed=13)
+    mm = pf.and_masks(pf.causal_mask, pf.tile_mask(table, 128))
+    o, lse = pf.flash_attention_fwd(q, k, v, mm)
+    assert torch.all(o[:, :, :128] == 0) and torch.all(torch.isneginf(lse[:, :, :128]))
+    check_all(q, k, v, do, mm, O.and_(O.causal, O.tile_table(table, 128)))
+
+
+def test_strided_layout_inputs():
+    """(B, T, H, D) storage viewed as (B, H, T, D): strides pass through the C ABI."""
+    rng = np.random.default_rng(14)
+    base = [torch.from_numpy(rng.standard_normal((2, 256, 4, 128)).astype(np.float32)).to(DEV, torch.bfloat16)
+            for _ in range(4)]
+    q, k, v, do = (t.transpose(1, 2) for t in base)
+    assert not q.is_contiguous()
+    check_all(q, k, v, do, pf.causal_mask, O.causal)
+
+
+def test_forward_is_deterministic():
+    q, k, v, do = inputs((2, 4, 1024, 128), (2, 4, 1024, 128), torch.bfloat16, seed=15)
+    o1, l1 = pf.flash_attention_fwd(q, k, v, pf.causal_mask)
+    o2, l2 = pf.flash_attention_fwd(q, k, v, pf.causal_mask)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+def test_block_mask_argument_and_reference_style_lists():
+    T = 512
+    q, k, v, do = inputs((1, 2, T, 128), (1, 2, T, 128), torch.bfloat16, seed=16)
+    bm = pf.create_block_mask(pf.causal_mask, 1, 2, T, T, 128)
+    check_all(q, k, v, do, None, O.causal, block_mask=bm)  # mask_mod taken from the block mask
+    lists = pf.create_causal_block_mask(T, 128)  # host-built, reference fields only: all tiles partial
+    check_all(q, k, v, do, pf.causal_mask, O.causal, block_mask=lists)
+
+
+def test_lse_matches_oracle():
+    q, k, v, do = inputs((1, 2, 300, 128), (1, 2, 300, 128), torch.bfloat16, seed=17)
+    _, lse = pf.flash_attention_fwd(q, k, v, pf.sliding_window_mask(40, 3))
+    _, rlse, _ = oracle(q, k, v, do, O.sliding_window(40, 3))
+    np.testing.assert_allclose(lse.cpu().numpy(), rlse, atol=2e-3, rtol=1e-4)
+
+
+# ------------------------------------------------------------------------ full-length benchmark shapes
+def torch_reference(q, k, v, do, mask_fn, score_fn=None, chunk=1024):
+    """Chunked fp32 reference on the GPU: o, lse, dq, dk, dv with the oracle's formulas."""
+    B, H, T, D = q.shape
+    s = 1.0 / math.sqrt(D)
+    qf, kf, vf, dof = (t.float() for t in (q, k, v, do))
+    o = torch.empty_like(qf)
+    lse = torch.empty(q.shape[:3], device=q.device)
+    kvi = torch.arange(k.shape[2], device=q.device)[None, :]
+    hi = torch.arange(H, device=q.device)[None, :, None, None]
+
+    def scores(r0, r1):
+        raw = torch.einsum("bhqd,bhkd->bhqk", qf[:, :, r0:r1], kf) * s
+        qi = torch.arange(r0, r1, device=q.device)[:, None]
+        x, g = raw, torch.ones_like(raw)
+        if score_fn is not None:
+            x, g = score_fn(raw, hi, qi, kvi)
+        m = mask_fn(qi, kvi) if mask_fn is not None else torch.ones_like(x, dtype=torch.bool)
+        return torch.where(m, x, torch.tensor(-math.inf, device=q.device)), g
+
+    for r0 in range(0, T, chunk):
+        x, _ = scores(r0, min(r0 + chunk, T))
+        l = torch.logsumexp(x, -1)
+        p = torch.exp(x - l[..., None]).nan_to_num(0.0)
+        o[:, :, r0:r0 + chunk] = p @ vf
+        lse[:, :, r0:r0 + chunk] = l
+    delta = (o * dof).sum(-1)
+    dq, dk, dv = torch.zeros_like(qf), torch.zeros_like(kf), torch.zeros_like(vf)
+    for r0 in range(0, T, chunk):
+        r1 = min(r0 + chunk, T)
+        x, g = scores(r0, r1)
+        p = torch.exp(x - lse[:, :, r0:r1, None]).nan_to_num(0.0)
+        dp = dof[:, :, r0:r1] @ vf.transpose(-1, -2)
+        ds = p * (dp - delta[:, :, r0:r1, None]) * g
+        dv += p.transpose(-1, -2) @ dof[:, :, r0:r1]
+        dk += ds.transpose(-1, -2) @ qf[:, :, r0:r1] * s
+        dq[:, :, r0:r1] = ds @ kf * s
+    return o, lse, dq, dk, dv
+
+
+def test_torch_reference_matches_oracle():
+    q, k, v, do = inputs((1, 2, 256, 64), (1, 2, 256, 64), torch.float32, seed=18)
+
+    def sc(raw, h, qi, ki):
+        t = torch.tanh(raw / 3.0)
+        return 3.0 * t, 1 - t * t
+
+    ro, rlse, rg = oracle(q, k, v, do, O.causal, (O.softcap(3.0),))
+    to, tlse, *tg = torch_reference(q, k, v, do, lambda qi, ki: qi >= ki, sc, chunk=100)
+    np.testing.assert_allclose(to.cpu().numpy(), ro, atol=1e-5)
+    for a, b in zip(tg, rg):
+        np.testing.assert_allclose(a.cpu().numpy(), b, atol=1e-4)
+
+
+@pytest.mark.parametrize("cfg", [2, 3, 4, 5])
+def test_benchmark_config_full_length(cfg):
+    """Each benchmark configuration at its full sequence length on two heads."""
+    w = W.get(cfg)
+    H = 2
+    g = torch.Generator(device=DEV).manual_seed(cfg)
+    q, k, v, do = (torch.randn((1, H, w.S, w.D), generator=g, device=DEV) * w.input_scale for _ in range(4))
+    q, k, v, do = (t.to(w.dtype) for t in (q, k, v, do))
+    mm, sm = w.mask_mod, w.score_mod
+    if cfg == 3:  # ALiBi slopes of the 32-head config, heads 0 and 1
+        sm = pf.alibi_score_mod(slopes=pf.alibi_slopes(32)[:H])
+    o, (dq, dk, dv) = run_api(q, k, v, do, mm, sm)
+
+    def score_fn(raw, hi, qi, ki):
+        if cfg == 3:
+            return raw + pf.alibi_slopes(32)[:H].to(DEV)[hi] * (ki - qi), torch.ones_like(raw)
+        if cfg == 5:
+            t = torch.tanh(raw / 30.0)
+            return 30.0 * t, 1 - t * t
+        return raw, torch.ones_like(raw)
+
+    ref = torch_reference(q, k, v, do, mm, score_fn if cfg in (3, 5) else None, chunk=512 if w.S > 8192 else 1024)
+    for n, a, b in zip(("o", "lse", "dq", "dk", "dv"), (o, None, dq, dk, dv), ref):
+        if a is not None:
+            close(n, a, b, torch.bfloat16)
