@@ -249,7 +249,9 @@ def main():
     FA.check_device_status(device)
     plan = FA._Plan(q.detach(), k.detach(), v.detach(), w.mask_mod, w.score_mod, None, 64, 64, 3, None, True)
     fwd_launches = 1
-    bwd_launches = 4  # preprocess + dQ kernel + dK/dV kernel + dQ convert (generic backward)
+    # tcgen05 backward: preprocess (delta, lse2, zeroed dQ accumulator) + fused kernel + dQ convert;
+    # generic backward: preprocess + dQ kernel + dK/dV kernel + dQ convert
+    bwd_launches = 3 if plan.kernel == FA.L.FA_KERNEL_AUTO else 4
 
     def timed(fn, n):
         barrier(dist)

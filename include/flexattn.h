@@ -63,32 +63,38 @@ enum {
  *   DOCUMENT    doc_q[b][q] == doc_kv[b][kv]              (mask_mod.py:46-59 stub, built here)
  *   TILE_TABLE  table[q / table_block][kv / table_block] != 0
  * No flag set = bidirectional (mask_mod.py:20-22).  Elements with kv >= Tkv are
- * always masked. */
+ * always masked.  Predicates (and the position-dependent score mods) see global
+ * positions q + q_offset and kv + kv_offset, so a caller can run one block of a
+ * longer sequence (the context-parallel ring does); document ids and the tile
+ * table are indexed by global position. */
 enum { FA_MASK_CAUSAL = 1, FA_MASK_WINDOW = 2, FA_MASK_DOCUMENT = 4, FA_MASK_TILE_TABLE = 8 };
 
 typedef struct {
   int32_t flags;
   int32_t window_left, window_right; /* -1 = unlimited */
-  const int32_t* doc_q;              /* [doc_b, Tq] device int32 document ids */
-  const int32_t* doc_kv;             /* [doc_b, Tkv] */
+  const int32_t* doc_q;              /* [doc_b, >= q_offset + Tq] device int32 document ids */
+  const int32_t* doc_kv;             /* [doc_b, >= kv_offset + Tkv] */
   int64_t doc_stride_b;              /* elements between batches; 0 = shared by all batches */
   const uint8_t* tile_table;         /* [table_rows, table_cols] device bytes, nonzero = keep */
   int32_t table_rows, table_cols, table_block;
+  int32_t q_offset, kv_offset;       /* global position of row 0 of q / of k, v */
 } FaMaskSpec;
 
 /* ------------------------------------------------------------------ score_mod registry
  * Applied in this order to the scaled logit s = scale * q.k:
  *   ALIBI     s += slope[h] * (kv - q)
- *   REL_BIAS  s += bias[h][q - kv + Tkv - 1]
- *   SOFTCAP   s  = cap * tanh(s / cap)   (backward multiplies by 1 - tanh^2) */
+ *   REL_BIAS  s += bias[h][q - kv + center]
+ *   SOFTCAP   s  = cap * tanh(s / cap)   (backward multiplies by 1 - tanh^2)
+ * with global positions q, kv (see FaMaskSpec offsets). */
 enum { FA_SCORE_ALIBI = 1, FA_SCORE_SOFTCAP = 2, FA_SCORE_REL_BIAS = 4 };
 
 typedef struct {
   int32_t flags;
   float softcap;
   const float* alibi_slopes; /* [H] device fp32 */
-  const float* rel_bias;     /* [H or 1, Tq + Tkv - 1] device fp32 */
+  const float* rel_bias;     /* [H or 1, L] device fp32, L covers every q - kv + center used */
   int64_t rel_bias_stride_h; /* 0 = one table for all heads */
+  int32_t rel_bias_center;   /* table index of q == kv; <= 0 means Tkv - 1 */
 } FaScoreSpec;
 
 /* ------------------------------------------------------------------ block tables
@@ -131,7 +137,8 @@ typedef struct {
   FaScoreSpec score;
   FaBlockTables blocks;
   int32_t kernel;           /* FA_KERNEL_* */
-  int32_t num_stages;       /* K/V pipeline depth for the tcgen05 kernel, 0 = default */
+  int32_t num_stages;       /* K/V entries in flight in the tcgen05 forward (each = K + V tile);
+                               0 = as many as shared memory holds */
   int32_t* status;          /* optional device int32: nonzero after a device-side timeout */
 } FaFwdParams;
 

@@ -59,6 +59,23 @@ int make_bf16_map(CUtensorMap* map, const FaTensor& t, int B, int heads, int T, 
   return FA_OK;
 }
 
+// 3-D map over the fp32 dQ accumulator [B*H, Tq, D]; box = 32 columns x 32 rows, 128-byte
+// swizzle (the layout the drain warps stage in shared memory).  Rows past Tq are out of
+// bounds, so reduce-adds of a partial last tile never touch the next head.
+int make_dq_accum_map(CUtensorMap* map, float* base, int BH, int Tq, int D) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Tq, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 4, (cuuint64_t)Tq * D * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ERR_INVALID, "tensor map for the dQ accumulator rejected (CUresult %d)", (int)r);
+  return FA_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_tensor(const FaTensor& t, const char* name, int elem) {
@@ -144,8 +161,10 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
     if (!tc_ok)
       return fail(FA_ERR_UNSUPPORTED,
                   "tcgen05 forward needs bf16, D in {64,128}, 128x128 block tables and 16-byte aligned rows");
+    // num_stages counts K/V entries in flight (the reference's pipelining depth); each
+    // entry takes two ring slots (K and V).  0 = as deep as shared memory allows.
     const int max_ns = fwd_tc_max_stages(p->D, p->blocks.nkv);
-    int ns = p->num_stages > 0 ? p->num_stages : 4;
+    int ns = p->num_stages > 0 ? 2 * p->num_stages : max_ns;
     if (ns < 2) ns = 2;
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
@@ -245,13 +264,14 @@ int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_str
     int ns = p->num_stages > 0 ? p->num_stages : 2;
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
-    CUtensorMap tq, tk, tv, tdo;
+    CUtensorMap tq, tk, tv, tdo, tdq;
     if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q")) ||
         (rc = make_bf16_map(&tk, p->k, p->B, p->H, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H, p->Tkv, p->D, "v")) ||
-        (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout")))
+        (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout")) ||
+        (rc = make_dq_accum_map(&tdq, a.dq_accum, p->B * p->H, p->Tq, p->D)))
       return rc;
-    e = launch_bwd_tc(a, tq, tk, tv, tdo, (cudaStream_t)stream);
+    e = launch_bwd_tc(a, tq, tk, tv, tdo, tdq, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_bwd (tcgen05)");
   } else if (kernel == FA_KERNEL_SIMT) {
     e = launch_bwd_simt(a, p->dtype, (cudaStream_t)stream);

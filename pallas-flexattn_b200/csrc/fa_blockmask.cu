@@ -1,4 +1,5 @@
-// GPU construction of FlexAttention block tables.
+// GPU construction of FlexAttention block tables.  Tile coordinates are local; the
+// mask sees global positions (q + q_offset, kv + kv_offset).
 //
 // classify_kernel replaces the host double loop of the reference's
 // create_block_mask (src/pallas_flexattn/block_mask.py:54-129), which evaluates the
@@ -38,8 +39,8 @@ __global__ void __launch_bounds__(kClassifyThreads)
       const int qs[3] = {q0, (q0 + q1) / 2, q1 - 1};
       const int ks[3] = {k0, (k0 + k1) / 2, k1 - 1};
       const int q = qs[threadIdx.x / 3], kv = ks[threadIdx.x % 3];
-      const int dq = (mc.flags & FA_MASK_DOCUMENT) ? mc.doc_q[q] : 0;
-      v = mask_ok(mc, q, kv, dq);
+      const int dq = (mc.flags & FA_MASK_DOCUMENT) ? mc.doc_q[q + mc.q_off] : 0;
+      v = mask_ok(mc, q + mc.q_off, kv + mc.kv_off, dq);
     }
     cls = __syncthreads_or(v) ? 1 : 0;
   } else {
@@ -52,8 +53,8 @@ __global__ void __launch_bounds__(kClassifyThreads)
         const int64_t idx = base + u * kClassifyThreads + threadIdx.x;
         if (idx >= n) break;
         const int q = q0 + (int)(idx / bkv), kv = k0 + (int)(idx % bkv);
-        const int dq = (mc.flags & FA_MASK_DOCUMENT) ? mc.doc_q[q] : 0;
-        const bool v = mask_ok(mc, q, kv, dq);
+        const int dq = (mc.flags & FA_MASK_DOCUMENT) ? mc.doc_q[q + mc.q_off] : 0;
+        const bool v = mask_ok(mc, q + mc.q_off, kv + mc.kv_off, dq);
         any = any || v;
         all = all && v;
       }

@@ -6,16 +6,17 @@
 //   St  = K Q_i^T          dPt = V dO_i^T          (TMEM, fp32)
 //   Pt  = exp2(score(St) - lse2_i)   dSt = Pt * (dPt - delta_i) * score'   (registers)
 //   dV += Pt dO_i  (A = Pt from TMEM)   dK += dSt Q_i   dQ_i = dS K   (fp32 in TMEM)
-// dQ_i is added into an fp32 accumulator in global memory by a dedicated warpgroup;
-// fa_bwd scales and converts it afterwards.  The CTA walks the transposed block
-// table (q_indices / full_q_indices) of its kv tile, skipping empty tiles; full
-// tiles do not evaluate the mask.
+// dQ_i is added into an fp32 accumulator in global memory with TMA reduce-add by a
+// dedicated warpgroup; fa_bwd scales and converts it afterwards.  The CTA walks the
+// transposed block table (q_indices / full_q_indices) of its kv tile, skipping empty
+// tiles; full tiles do not evaluate the mask.
 //
-// Warp roles (448 threads):
-//   warps 0-7   compute: thread = kv row; warps 0-3 take q columns 0-63, 4-7 take 64-127
-//   warps 8-11  dQ drain: thread = q row; TMEM -> fp32 vector atomics
-//   warp 12     TMA producer (K, V once; then Q_i + lse2_i and dO_i + delta_i rings)
-//   warp 13     MMA issuer + TMEM owner
+// Warp roles (512 threads, four warpgroups):
+//   WG0, WG1 (warps 0-7)  compute: thread = kv row; WG0 takes q columns 0-63, WG1 64-127
+//   WG2 (warps 8-11)      dQ drain: thread = q row; TMEM -> swizzled smem -> TMA reduce-add
+//   WG3 (warps 12-15)     warp 12 TMA producer, warp 13 MMA issuer + TMEM owner, 14-15 idle
+// Registers: launched at 128 per thread (512 x 128 = 65536); setmaxnreg moves them to
+// 176 for WG0/WG1, 96 for WG2, 64 for WG3 (2*128*176 + 128*96 + 128*64 = 65536).
 // TMEM columns: St [0,128) (Pt bf16 written back into its own half), dPt [128,256)
 // (reused for dQ_i once dSt is in shared memory), dV [256,256+D), dK [256+D,256+2D).
 // dSt is stored once in shared memory in the 128-byte-swizzled K-major layout; the
@@ -34,13 +35,15 @@ namespace {
 
 constexpr int kBM = 128;  // kv rows per CTA
 constexpr int kBQ = 128;  // q rows per iteration
-constexpr int kBwdThreads = 448;
+constexpr int kBwdThreads = 512;
 constexpr int kWarpDq0 = 8, kWarpProd = 12, kWarpMma = 13;
-constexpr int kChunk = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row tile
+constexpr int kRegsCompute = 176, kRegsDrain = 96, kRegsCtl = 64;
+constexpr int kChunk = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row bf16 tile
+constexpr int kDqStage = 32 * 32 * 4;  // per drain warp: 32 rows x 32 fp32, 128B-swizzled
 
 struct BwdSmemLayout {
-  int tile, nq_st, no_st, k_off, v_off, q_off, o_off, ds_off, lse_off, dl_off, bar_off, misc_off, cls_off, ent_off,
-      total;
+  int tile, nq_st, no_st, k_off, v_off, q_off, o_off, ds_off, dq_off, lse_off, dl_off, bar_off, misc_off, cls_off,
+      ent_off, total;
 };
 
 __host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int no_st, int nq) {
@@ -53,7 +56,8 @@ __host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int n
   L.q_off = 2 * L.tile;
   L.o_off = L.q_off + nq_st * L.tile;
   L.ds_off = L.o_off + no_st * L.tile;
-  L.lse_off = L.ds_off + kBQ * kBM * 2;
+  L.dq_off = L.ds_off + kBQ * kBM * 2;
+  L.lse_off = L.dq_off + 4 * kDqStage;
   L.dl_off = L.lse_off + nq_st * kBQ * 4;
   L.bar_off = L.dl_off + nq_st * kBQ * 4;
   L.misc_off = L.bar_off + (2 * nq_st + 2 * no_st + 12) * 8;
@@ -67,7 +71,7 @@ template <int D, int SK>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                  const AttnArgs a, const int NQS, const int NOS) {
+                  const __grid_constant__ CUtensorMap tm_dq, const AttnArgs a, const int NQS, const int NOS) {
   constexpr int NCHUNK = D / 64;
   constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DV = 256, TM_DK = 256 + D;
   constexpr uint32_t IDESC_SQ = make_idesc_bf16(kBM, kBQ, 0, 0);  // St, dPt: N = q
@@ -83,6 +87,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sQ = smem + L.q_off;
   uint8_t* sO = smem + L.o_off;
   uint8_t* sdS = smem + L.ds_off;
+  uint8_t* sDq = smem + L.dq_off;
   float* sLse = reinterpret_cast<float*>(smem + L.lse_off);
   float* sDl = reinterpret_cast<float*>(smem + L.dl_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -139,6 +144,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == kWarpMma) {
     tmem_alloc(tmem_base_s, 512);
@@ -178,149 +184,169 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem_base = *tmem_base_s;
   const int n_ent = *n_entries_s;
 
-  if (warp == kWarpProd) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0 && n_ent > 0) {
-      mbar_arrive_expect_tx(bar_kv, 2 * L.tile);
-      for (int c = 0; c < NCHUNK; ++c) {
-        tma_load_4d(sK + c * kChunk, &tm_k, bar_kv, c * 64, j * kBM, h, b);
-        tma_load_4d(sV + c * kChunk, &tm_v, bar_kv, c * 64, j * kBM, h, b);
+  if (warp >= kWarpProd) {
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == kWarpProd) {
+      // ---------------------------------------------------------------- TMA producer
+      if (lane == 0 && n_ent > 0) {
+        mbar_arrive_expect_tx(bar_kv, 2 * L.tile);
+        for (int c = 0; c < NCHUNK; ++c) {
+          tma_load_4d(sK + c * kChunk, &tm_k, bar_kv, c * 64, j * kBM, h, b);
+          tma_load_4d(sV + c * kChunk, &tm_v, bar_kv, c * 64, j * kBM, h, b);
+        }
+        const float* lse2 = a.lse2 + (int64_t)bh * Tq_pad;
+        const float* dl = a.delta + (int64_t)bh * Tq_pad;
+        bool ok = true;
+        int issued_q = 0, issued_o = 0;
+        for (int t = 0; t < n_ent && ok; ++t) {
+          const int i = entries[t] & 0xFFFFFF;
+          const int qs = t % NQS, qu = t / NQS;
+          if (!mbar_wait(bar_q_empty + qs, (qu & 1) ^ 1, abort_flag)) { ok = false; break; }
+          // lse2 and delta ride with Q: the Q slot is released only after dSt is built, which
+          // is the last read of both (the dO slot is released earlier, after the dV MMA).
+          mbar_arrive_expect_tx(bar_q_full + qs, L.tile + 2 * kBQ * 4);
+          for (int c = 0; c < NCHUNK; ++c)
+            tma_load_4d(sQ + qs * L.tile + c * kChunk, &tm_q, bar_q_full + qs, c * 64, i * kBQ, h, b);
+          bulk_load(sLse + qs * kBQ, lse2 + i * kBQ, kBQ * 4, bar_q_full + qs);
+          bulk_load(sDl + qs * kBQ, dl + i * kBQ, kBQ * 4, bar_q_full + qs);
+          ++issued_q;
+          const int os = t % NOS, ou = t / NOS;
+          if (!mbar_wait(bar_o_empty + os, (ou & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar_o_full + os, L.tile);
+          for (int c = 0; c < NCHUNK; ++c)
+            tma_load_4d(sO + os * L.tile + c * kChunk, &tm_do, bar_o_full + os, c * 64, i * kBQ, h, b);
+          ++issued_o;
+        }
+        if (!ok) {
+          report_status(a.status, FA_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        // Teardown: no bulk copy may still be writing this CTA's shared memory.
+        volatile int never = 0;
+        mbar_wait(bar_kv, 0, &never);
+        for (int s = 0; s < NQS && s < issued_q; ++s) {
+          const int last = s + ((issued_q - 1 - s) / NQS) * NQS;
+          mbar_wait(bar_q_full + s, (last / NQS) & 1, &never);
+        }
+        for (int s = 0; s < NOS && s < issued_o; ++s) {
+          const int last = s + ((issued_o - 1 - s) / NOS) * NOS;
+          mbar_wait(bar_o_full + s, (last / NOS) & 1, &never);
+        }
       }
-      const float* lse2 = a.lse2 + (int64_t)bh * Tq_pad;
-      const float* dl = a.delta + (int64_t)bh * Tq_pad;
-      bool ok = true;
-      int issued_q = 0, issued_o = 0;
-      for (int t = 0; t < n_ent && ok; ++t) {
-        const int i = entries[t] & 0xFFFFFF;
-        const int qs = t % NQS, qu = t / NQS;
-        if (!mbar_wait(bar_q_empty + qs, (qu & 1) ^ 1, abort_flag)) { ok = false; break; }
-        // lse2 and delta ride with Q: the Q slot is released only after dSt is built, which
-        // is the last read of both (the dO slot is released earlier, after the dV MMA).
-        mbar_arrive_expect_tx(bar_q_full + qs, L.tile + 2 * kBQ * 4);
-        for (int c = 0; c < NCHUNK; ++c)
-          tma_load_4d(sQ + qs * L.tile + c * kChunk, &tm_q, bar_q_full + qs, c * 64, i * kBQ, h, b);
-        bulk_load(sLse + qs * kBQ, lse2 + i * kBQ, kBQ * 4, bar_q_full + qs);
-        bulk_load(sDl + qs * kBQ, dl + i * kBQ, kBQ * 4, bar_q_full + qs);
-        ++issued_q;
-        const int os = t % NOS, ou = t / NOS;
-        if (!mbar_wait(bar_o_empty + os, (ou & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(bar_o_full + os, L.tile);
-        for (int c = 0; c < NCHUNK; ++c)
-          tma_load_4d(sO + os * L.tile + c * kChunk, &tm_do, bar_o_full + os, c * 64, i * kBQ, h, b);
-        ++issued_o;
+    } else if (warp == kWarpMma) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0 && n_ent > 0) {
+        // Descriptors are built once; per K step only the start-address field of the low
+        // word moves (see mma_ss_lh).  K-major: LBO 16 B; MN-major: LBO = one 64-column
+        // panel; SBO = 1024 B for both.  kofs/mofs are the per-step offsets in 16-byte units.
+        const uint64_t d0 = make_smem_desc(smem_u32(sK), 16, 1024, SMEM_SWIZZLE_128B);
+        const uint32_t hi = (uint32_t)(d0 >> 32);
+        const uint32_t kmaj = (uint32_t)d0 - ((smem_u32(sK) >> 4) & 0x3FFFu);  // LBO bits only
+        const uint32_t mnmaj = (uint32_t)make_smem_desc(0, kChunk, 1024, SMEM_SWIZZLE_128B);
+        auto lo = [](uint32_t lbo_bits, const void* p) { return lbo_bits + ((smem_u32(p) >> 4) & 0x3FFFu); };
+        const uint32_t K_k = lo(kmaj, sK), K_mn = lo(mnmaj, sK), V_k = lo(kmaj, sV), S_k = lo(kmaj, sdS),
+                       S_mn = lo(mnmaj, sdS);
+        const uint32_t Q_k0 = lo(kmaj, sQ), Q_mn0 = lo(mnmaj, sQ), O_k0 = lo(kmaj, sO), O_mn0 = lo(mnmaj, sO);
+        const uint32_t tile16 = (uint32_t)L.tile >> 4;
+        auto kofs = [](int kk) { return (uint32_t)((kk >> 2) * (kChunk >> 4) + (kk & 3) * 2); };
+        auto mofs = [](int kk) { return (uint32_t)(kk * (2048 >> 4)); };
+        bool ok = mbar_wait(bar_kv, 0, abort_flag);
+        tc_fence_after();
+        for (int t = 0; t < n_ent && ok; ++t) {
+          const int qs = t % NQS, os = t % NOS;
+          const uint32_t ph = t & 1;
+          const uint32_t Q_k = Q_k0 + qs * tile16, Q_mn = Q_mn0 + qs * tile16;
+          const uint32_t O_k = O_k0 + os * tile16, O_mn = O_mn0 + os * tile16;
+          const uint32_t acc0 = t > 0 ? 1u : 0u;
+          // St = K Q^T
+          if (!(ok = mbar_wait(bar_q_full + qs, (t / NQS) & 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss_lh(tmem_base + TM_S, K_k + kofs(kk), hi, Q_k + kofs(kk), hi, IDESC_SQ, kk > 0);
+          tc_commit(bar_s_full);
+          // dPt = V dO^T (its columns also hold dQ of the previous step until drained)
+          if (!(ok = mbar_wait(bar_o_full + os, (t / NOS) & 1, abort_flag))) break;
+          if (t > 0 && !(ok = mbar_wait(bar_dq_empty, ph ^ 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss_lh(tmem_base + TM_DP, V_k + kofs(kk), hi, O_k + kofs(kk), hi, IDESC_SQ, kk > 0);
+          tc_commit(bar_dp_full);
+          // dV += Pt dO  (Pt of q columns 0-63 at St cols 0-31, 64-127 at cols 64-95)
+          if (!(ok = mbar_wait(bar_p_full, ph, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBQ / 16; ++kk)
+            mma_ts_lh(tmem_base + TM_DV, tmem_base + TM_S + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), O_mn + mofs(kk),
+                      hi, IDESC_KV, kk > 0 ? 1u : acc0);
+          tc_commit(bar_o_empty + os);
+          // dK += dSt Q ; dQ_i = dS K
+          if (!(ok = mbar_wait(bar_ds_full, ph, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBQ / 16; ++kk)
+            mma_ss_lh(tmem_base + TM_DK, S_k + kofs(kk), hi, Q_mn + mofs(kk), hi, IDESC_KV, kk > 0 ? 1u : acc0);
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            mma_ss_lh(tmem_base + TM_DP, S_mn + mofs(kk), hi, K_mn + mofs(kk), hi, IDESC_DQ, kk > 0);
+          tc_commit(bar_q_empty + qs);
+          tc_commit(bar_ds_empty);
+          tc_commit(bar_dq_full);
+        }
+        if (ok) tc_commit(bar_dkv_full);
+        if (!ok) {
+          report_status(a.status, FA_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        tc_commit(bar_teardown);
+        volatile int never = 0;
+        mbar_wait(bar_teardown, 0, &never);
       }
-      if (!ok) {
-        report_status(a.status, FA_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-      // Teardown: no bulk copy may still be writing this CTA's shared memory.
-      volatile int never = 0;
-      mbar_wait(bar_kv, 0, &never);
-      for (int s = 0; s < NQS && s < issued_q; ++s) {
-        const int last = s + ((issued_q - 1 - s) / NQS) * NQS;
-        mbar_wait(bar_q_full + s, (last / NQS) & 1, &never);
-      }
-      for (int s = 0; s < NOS && s < issued_o; ++s) {
-        const int last = s + ((issued_o - 1 - s) / NOS) * NOS;
-        mbar_wait(bar_o_full + s, (last / NOS) & 1, &never);
-      }
+      __syncwarp();
     }
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_ent > 0) {
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aO = smem_u32(sO), aS = smem_u32(sdS);
-      auto kdesc = [](uint32_t base, int kk) {  // K-major, 128B swizzle; kk = 16-element K step
-        return make_smem_desc(base + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024, SMEM_SWIZZLE_128B);
-      };
-      auto mndesc = [](uint32_t base, int kk) {  // MN-major, 128B swizzle; kk = 16-row K step
-        return make_smem_desc(base + kk * 2048, kChunk, 1024, SMEM_SWIZZLE_128B);
-      };
-      bool ok = mbar_wait(bar_kv, 0, abort_flag);
-      tc_fence_after();
-      for (int t = 0; t < n_ent && ok; ++t) {
-        const int qs = t % NQS, os = t % NOS;
-        const uint32_t ph = t & 1;
-        const uint32_t qa = aQ + qs * L.tile, oa = aO + os * L.tile;
-        // St = K Q^T
-        if (!(ok = mbar_wait(bar_q_full + qs, (t / NQS) & 1, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tmem_base + TM_S, kdesc(aK, kk), kdesc(qa, kk), IDESC_SQ, kk > 0);
-        tc_commit(bar_s_full);
-        // dPt = V dO^T (its columns also hold dQ of the previous step until drained)
-        if (!(ok = mbar_wait(bar_o_full + os, (t / NOS) & 1, abort_flag))) break;
-        if (t > 0 && !(ok = mbar_wait(bar_dq_empty, ph ^ 1, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tmem_base + TM_DP, kdesc(aV, kk), kdesc(oa, kk), IDESC_SQ, kk > 0);
-        tc_commit(bar_dp_full);
-        // dV += Pt dO  (Pt of q columns 0-63 at St cols 0-31, 64-127 at cols 64-95)
-        if (!(ok = mbar_wait(bar_p_full, ph, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBQ / 16; ++kk)
-          mma_ts(tmem_base + TM_DV, tmem_base + TM_S + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), mndesc(oa, kk),
-                 IDESC_KV, (t > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(bar_o_empty + os);
-        // dK += dSt Q ; dQ_i = dS K
-        if (!(ok = mbar_wait(bar_ds_full, ph, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBQ / 16; ++kk)
-          mma_ss(tmem_base + TM_DK, kdesc(aS, kk), mndesc(qa, kk), IDESC_KV, (t > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          mma_ss(tmem_base + TM_DP, mndesc(aS, kk), mndesc(aK, kk), IDESC_DQ, kk > 0);
-        tc_commit(bar_q_empty + qs);
-        tc_commit(bar_ds_empty);
-        tc_commit(bar_dq_full);
-      }
-      if (ok) tc_commit(bar_dkv_full);
-      if (!ok) {
-        report_status(a.status, FA_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-      tc_commit(bar_teardown);
-      volatile int never = 0;
-      mbar_wait(bar_teardown, 0, &never);
-    }
-    __syncwarp();
   } else if (warp >= kWarpDq0) {
+    setmaxnreg_dec<kRegsDrain>();
     // ------------------------------------------------------------------ dQ drain (thread = q row)
     const int wq = warp & 3;
-    const int r = wq * 32 + lane;
     const uint32_t t_dq = tmem_base + ((uint32_t)(wq * 32) << 16) + TM_DP;
+    uint8_t* stage = sDq + wq * kDqStage;
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int i = entries[t] & 0xFFFFFF;
       if (!(ok = mbar_wait(bar_dq_full, t & 1, abort_flag))) break;
       tc_fence_after();
-      const int q = i * kBQ + r;
-      float* dst = a.dq_accum + ((int64_t)bh * a.Tq + q) * D;
 #pragma unroll 1
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(t_dq + c0, v);
         tmem_ld_wait();
         reg_pin(v);
-        if (q < a.Tq) {
+        if (c0 + 32 == D) {  // all of dQ_i is in registers: its TMEM columns may be reused
+          tc_fence_before();
+          mbar_arrive(bar_dq_empty);
+        }
+        if (lane == 0) bulk_wait_read_all();  // the previous reduce has read the stage
+        __syncwarp();
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            atomicAdd(reinterpret_cast<float4*>(dst + c0 + 4 * u),
-                      make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
-                                  __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3])));
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tm_dq, stage, c0, i * kBQ + wq * 32, bh);
+          bulk_commit_group();
         }
       }
-      tc_fence_before();
-      mbar_arrive(bar_dq_empty);
     }
+    if (lane == 0) bulk_wait_all();
     if (!ok) {
       report_status(a.status, FA_ERR_TIMEOUT);
       *abort_flag = 1;
     }
   } else {
+    setmaxnreg_inc<kRegsCompute>();
     // ------------------------------------------------------------------ compute (thread = kv row)
     const int wg = warp >> 2;
     const int wq = warp & 3;
@@ -330,12 +356,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
+    const int kvg = kv + mc.kv_off;
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];
       const int i = e & 0xFFFFFF;
       const bool partial = ((e >> 24) & 3) == 1;
-      const int qs = t % NQS, os = t % NOS;
+      const int qs = t % NQS;
       const uint32_t ph = t & 1;
       const float* lse2 = sLse + qs * kBQ + cbase;
       const float* dl = sDl + qs * kBQ + cbase;
@@ -345,28 +372,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       float p[64];
       uint32_t g2[(SK == SC_SOFTCAP || SK == SC_GENERAL) ? 32 : 1];
-      {
-        uint32_t s0[32], s1[32];
-        tmem_ld32(t_lane + TM_S + cbase, s0);
-        tmem_ld32(t_lane + TM_S + cbase + 32, s1);
-        tmem_ld_wait();
-        reg_pin(s0);
-        reg_pin(s1);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float sraw = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]);
-          const int q = q0 + c;
-          const float x = score_log2<SK>(sraw, q, kv, sc);
-          float pv = ex2_approx(x - lse2[c]);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t s[32];
+        tmem_ld32(t_lane + TM_S + cbase + 32 * hh, s);
+        tmem_ld_wait();
+        reg_pin(s);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int cc = 32 * hh + c;
+          const int q = q0 + cc;            // local row
+          const int qg = q + mc.q_off;      // global positions for the mask and score mods
+          const float x = score_log2<SK>(__uint_as_float(s[c]), qg, kvg, sc);
+          float pv = ex2_approx(x - lse2[cc]);
           if (partial) {
-            const int dq = (mc.flags & FA_MASK_DOCUMENT) && q < a.Tq ? __ldg(mc.doc_q + q) : 0;
-            if (!mask_ok(mc, q, kv, dq)) pv = 0.f;
+            const int dq = (mc.flags & FA_MASK_DOCUMENT) && q < a.Tq ? __ldg(mc.doc_q + qg) : 0;
+            if (!mask_ok(mc, qg, kvg, dq)) pv = 0.f;
           }
-          p[c] = pv;
+          p[cc] = pv;
           if constexpr (SK == SC_SOFTCAP || SK == SC_GENERAL) {
             const float gv = score_grad<SK>(x, sc);
-            if (c & 1) g2[c >> 1] = pack_bf16x2(__uint_as_float(g2[c >> 1]), gv);
-            else g2[c >> 1] = __float_as_uint(gv);
+            if (cc & 1) g2[cc >> 1] = pack_bf16x2(__uint_as_float(g2[cc >> 1]), gv);
+            else g2[cc >> 1] = __float_as_uint(gv);
           }
         }
       }
@@ -488,7 +515,7 @@ int bwd_tc_max_stages(int D, int nq) {
 }
 
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          const CUtensorMap& tdo, cudaStream_t stream) {
+                          const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream) {
   int nqs = 0, nos = 0;
   if (!pick_stages(a.D, a.bt.nq, &nqs, &nos)) return cudaErrorInvalidValue;
   if (a.num_stages > 0 && a.num_stages < nqs) nqs = a.num_stages;
@@ -496,9 +523,15 @@ cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   const dim3 grid((unsigned)(a.bt.nkv * a.B * a.H));
   const int sk = score_kind_of(a.score.flags);
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.
+    cudaFuncAttributes fa_attr;
+    cudaError_t e = cudaFuncGetAttributes(&fa_attr, kern);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kBwdThreads, smem, stream>>>(tq, tk, tv, tdo, a, nqs, nos);
+    if (fa_attr.numRegs * kBwdThreads < 2 * 128 * kRegsCompute + 128 * kRegsDrain + 128 * kRegsCtl)
+      return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kBwdThreads, smem, stream>>>(tq, tk, tv, tdo, tdq, a, nqs, nos);
     return cudaGetLastError();
   };
 #define FA_BWD_CASE(DD, SKK) \

@@ -48,7 +48,7 @@ __device__ inline ScoreCtx make_score_ctx(const FaScoreSpec& s, float scale, int
   c.cap_log2 = c.cap * kLog2e;
   c.inv_cap = 1.f / c.cap;
   c.bias = (s.flags & FA_SCORE_REL_BIAS) ? s.rel_bias + (int64_t)h * s.rel_bias_stride_h : nullptr;
-  c.bias_off = Tkv - 1;
+  c.bias_off = s.rel_bias_center > 0 ? s.rel_bias_center : Tkv - 1;
   return c;
 }
 
@@ -89,9 +89,11 @@ __device__ __forceinline__ float score_grad(float x_log2, const ScoreCtx& c) {
   }
 }
 
-// Per-(b) mask context.
+// Per-(b) mask context.  Predicates take GLOBAL positions (local + q_off / kv_off);
+// Tkv holds the global end of the key range (kv_off + Tkv).
 struct MaskCtx {
   int flags, left, right, Tkv;
+  int q_off, kv_off;
   const int32_t* doc_q;   // row of batch b
   const int32_t* doc_kv;
   const uint8_t* table;
@@ -103,7 +105,9 @@ __device__ inline MaskCtx make_mask_ctx(const FaMaskSpec& m, int b, int Tkv) {
   c.flags = m.flags;
   c.left = m.window_left;
   c.right = m.window_right;
-  c.Tkv = Tkv;
+  c.q_off = m.q_offset;
+  c.kv_off = m.kv_offset;
+  c.Tkv = m.kv_offset + Tkv;
   c.doc_q = (m.flags & FA_MASK_DOCUMENT) ? m.doc_q + (int64_t)b * m.doc_stride_b : nullptr;
   c.doc_kv = (m.flags & FA_MASK_DOCUMENT) ? m.doc_kv + (int64_t)b * m.doc_stride_b : nullptr;
   c.table = m.tile_table;
@@ -112,7 +116,8 @@ __device__ inline MaskCtx make_mask_ctx(const FaMaskSpec& m, int b, int Tkv) {
   return c;
 }
 
-// mask_mod(q, kv) for one element. `dq` is doc_q[q] (ignored without DOCUMENT).
+// mask_mod(q, kv) for one element at global positions. `dq` is doc_q[q] (ignored
+// without DOCUMENT).
 __device__ __forceinline__ bool mask_ok(const MaskCtx& m, int q, int kv, int dq) {
   bool ok = kv < m.Tkv;
   if (m.flags & FA_MASK_CAUSAL) ok = ok && (q >= kv);

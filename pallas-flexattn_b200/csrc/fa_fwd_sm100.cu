@@ -13,15 +13,17 @@
 //   * the logsumexp is fp32 (the reference stores it in the input dtype,
 //     flash_attn.py:144).
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads, three warpgroups):
 //   warps 0-3  softmax for Q sub-tile 0 (thread = row)     warps 4-7  sub-tile 1
 //   warp 8     TMA producer (Q once, then K_j, V_j into an NS-slot ring)
-//   warp 9     MMA issuer (one thread) + TMEM owner
+//   warps 9/10 MMA issuers for sub-tiles 0/1 (one thread each); warp 9 owns TMEM; warp 11 idle
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
-// Per kv entry t the MMA thread issues PV_i(t) then S_i(t+1) for i = 0, 1, so one
+// Per kv entry t the issuer of sub-tile i issues PV_i(t) then S_i(t+1), so one
 // sub-tile's softmax overlaps the other's tensor-core work.  Because tcgen05 ops of
 // one thread complete in issue order, the arrival of S_i(t+1) also proves PV_i(t)
 // is done, which is what lets the softmax warps rescale O without another barrier.
+// (A single issuing thread for both sub-tiles was measured to leave the tensor pipe
+// idle between MMA groups: its serial chain of waits and commits was the bottleneck.)
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -36,7 +38,24 @@ namespace {
 
 constexpr int kBM = 128;          // rows of one Q sub-tile
 constexpr int kBN = 128;          // rows of one K/V tile
-constexpr int kFwdThreads = 320;  // 8 softmax warps + producer + MMA
+constexpr int kFwdThreads = 384;  // 3 warpgroups: 2 softmax + (producer, MMA, 2 idle)
+// setmaxnreg split: the launch gives every thread 168 registers (384 x 168 = 64512);
+// the softmax warpgroups take 216 and the control warpgroup keeps 72 (2*128*216 + 128*72
+// = 64512).  launch_fwd_tc checks the launch allocation before every launch.
+constexpr int kRegsSoftmax = 216, kRegsCtl = 72;
+// Of every 4 exponential pairs in a full tile, this many run as a polynomial on the FMA
+// pipes instead of the MUFU pipe.
+#ifndef FA_FWD_EXP_EMU
+#define FA_FWD_EXP_EMU 0
+#endif
+// Softmax ping-pong: -1 chooses per launch, 0 forces it off, 1 forces it on.
+#ifndef FA_FWD_PINGPONG
+#define FA_FWD_PINGPONG -1
+#endif
+// P is packed to bf16 with integer ops (1) or with cvt.rn.bf16x2.f32 (0).
+#ifndef FA_FWD_INT_PACK
+#define FA_FWD_INT_PACK 0
+#endif
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct FwdSmemLayout {
@@ -49,7 +68,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv)
   L.q_off = 0;
   L.kv_off = 2 * L.tile_bytes;
   L.bar_off = L.kv_off + ns * L.tile_bytes;
-  L.misc_off = L.bar_off + (2 * ns + 8) * 8;
+  L.misc_off = L.bar_off + (2 * ns + 12) * 8;
   L.cls_off = L.misc_off + 16;
   L.ent_off = L.cls_off + 4 * nkv;
   L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
@@ -59,7 +78,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv)
 template <int D, int SK>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int pingpong) {
   constexpr int CHUNK_BYTES = kBM * 64 * 2;  // one 64-column, 128-byte-swizzled panel
   constexpr int NCHUNK = D / 64;
   constexpr uint32_t TM_S0 = 0, TM_O0 = 256;
@@ -81,7 +100,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* bar_s_full = bars + 1 + 2 * NS;   // [2]
   uint64_t* bar_p_full = bar_s_full + 2;       // [2]
   uint64_t* bar_o_full = bar_p_full + 2;       // [2]
-  uint64_t* bar_teardown = bar_o_full + 2;
+  uint64_t* bar_teardown = bar_o_full + 2;     // [2]
+  uint64_t* bar_turn = bar_teardown + 2;       // [2] softmax ping-pong
   int* misc = reinterpret_cast<int*>(smem + L.misc_off);
   volatile int* abort_flag = misc;             // misc[0]
   int* n_entries_s = misc + 1;
@@ -102,7 +122,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(bar_q, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_kv_full + s, 1);
-      mbar_init(bar_kv_empty + s, 1);
+      mbar_init(bar_kv_empty + s, 2);  // released by both MMA issuers
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + i, 1);
@@ -110,6 +130,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(bar_o_full + i, 1);
     }
     mbar_init(bar_teardown, 1);
+    mbar_init(bar_teardown + 1, 1);
+    mbar_init(bar_turn, 128);
+    mbar_init(bar_turn + 1, 128);
     misc[0] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -168,6 +191,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t tmem_base = *tmem_base_s;
   const int n_ent = *n_entries_s;
 
+  if (warp >= 8) {
+  setmaxnreg_dec<kRegsCtl>();
   if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_ent > 0) {
@@ -201,77 +226,93 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mbar_wait(bar_kv_full + s, (last / NS) & 1, &never);
       }
     }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp == 9 || warp == 10) {
+    // ---------------------------------------------------------------- MMA issuers
+    // One issuing thread per Q sub-tile (warp 9: sub-tile 0, warp 10: sub-tile 1), so each
+    // thread's serial chain of waits, MMAs and commits covers half the work.  Both walk
+    // every kv entry and both commit to the K/V "empty" barriers (initialised with count
+    // 2), so a slot is released only after both sub-tiles' MMAs that read it retired.
+    const int i = warp - 9;
     if (lane == 0 && n_ent > 0) {
       const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
-      int last_t[2] = {-1, -1};
+      int last_t = -1;
       for (int t = 0; t < n_ent; ++t)
-        for (int i = 0; i < 2; ++i)
-          if ((entries[t] >> (24 + 2 * i)) & 3) last_t[i] = t;
+        if ((entries[t] >> (24 + 2 * i)) & 3) last_t = t;
       bool ok = mbar_wait(bar_q, 0, abort_flag);
       tc_fence_after();
-      uint32_t p_phase[2] = {0, 0};
-      int pv_count[2] = {0, 0};
+      uint32_t p_phase = 0;
+      int pv_count = 0;
 
-      auto issue_s = [&](int i, int t) -> bool {
+      // Descriptors are built once; per K step only the start-address field of the low
+      // word moves (see mma_ss_lh).  K-major operands (Q, K) use LBO 16 B, the MN-major
+      // V operand uses LBO = one 64-column panel; both use SBO = 1024 B (8 swizzled rows).
+      const uint64_t dq_base = make_smem_desc(sQa, 16, 1024, SMEM_SWIZZLE_128B);
+      const uint32_t desc_hi = (uint32_t)(dq_base >> 32);
+      const uint32_t tile16 = (uint32_t)L.tile_bytes >> 4;
+      const uint32_t q_lo = (uint32_t)dq_base + i * tile16;
+      const uint32_t k_lo0 = (uint32_t)make_smem_desc(sKVa, 16, 1024, SMEM_SWIZZLE_128B);
+      const uint32_t v_lo0 = (uint32_t)make_smem_desc(sKVa, CHUNK_BYTES, 1024, SMEM_SWIZZLE_128B);
+      const uint32_t s_dst = tmem_base + TM_S0 + 128 * i, o_dst = tmem_base + TM_O0 + D * i;
+
+      // S_i(t) = Q_i K_t^T (if this sub-tile visits entry t), then release K_t's slot.
+      auto issue_s = [&](int t, bool part) -> bool {
         const int slot = (2 * t) % NS;
         if (!mbar_wait(bar_kv_full + slot, ((2 * t) / NS) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t qa = sQa + i * L.tile_bytes, ka = sKVa + slot * L.tile_bytes;
+        if (part) {
+          tc_fence_after();
+          const uint32_t klo = k_lo0 + slot * tile16;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          mma_ss(tmem_base + TM_S0 + 128 * i, make_smem_desc(qa + off, 16, 1024, SMEM_SWIZZLE_128B),
-                 make_smem_desc(ka + off, 16, 1024, SMEM_SWIZZLE_128B), IDESC_S, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            constexpr uint32_t kChunk16 = CHUNK_BYTES >> 4;
+            const uint32_t off = (kk >> 2) * kChunk16 + (kk & 3) * 2;
+            mma_ss_lh(s_dst, q_lo + off, desc_hi, klo + off, desc_hi, IDESC_S, kk > 0);
+          }
+          tc_commit(bar_s_full + i);
         }
-        tc_commit(bar_s_full + i);
+        tc_commit(bar_kv_empty + slot);
         return true;
       };
-      auto issue_pv = [&](int i, int t) -> bool {
+      // O_i += P_i V_t (if visited), then release V_t's slot.  The slot's load is awaited
+      // even when this sub-tile skips the entry: a release may only follow the load of the
+      // same use, so neither thread can release a slot's next use before the other has
+      // released the current one (the empty barrier counts two arrivals per use).
+      auto issue_pv = [&](int t, bool part) -> bool {
         const int slot = (2 * t + 1) % NS;
         if (!mbar_wait(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
-        if (!mbar_wait(bar_p_full + i, p_phase[i], abort_flag)) return false;
-        p_phase[i] ^= 1;
-        tc_fence_after();
-        const uint32_t va = sKVa + slot * L.tile_bytes;
+        if (part) {
+          if (!mbar_wait(bar_p_full + i, p_phase, abort_flag)) return false;
+          p_phase ^= 1;
+          tc_fence_after();
+          const uint32_t vlo = v_lo0 + slot * tile16;
+          const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          mma_ts(tmem_base + TM_O0 + D * i, tmem_base + TM_S0 + 128 * i + kk * 8,
-                 make_smem_desc(va + kk * 2048, CHUNK_BYTES, 1024, SMEM_SWIZZLE_128B), IDESC_PV,
-                 (pv_count[i] > 0 || kk > 0) ? 1u : 0u);
-        ++pv_count[i];
-        if (t == last_t[i]) tc_commit(bar_o_full + i);
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_ts_lh(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+          ++pv_count;
+          if (t == last_t) tc_commit(bar_o_full + i);
+        }
+        tc_commit(bar_kv_empty + slot);
         return true;
       };
 
-      if (ok) {
-        for (int i = 0; i < 2 && ok; ++i)
-          if ((entries[0] >> (24 + 2 * i)) & 3) ok = issue_s(i, 0);
-        if (ok) tc_commit(bar_kv_empty + 0);
-      }
+      if (ok) ok = issue_s(0, ((entries[0] >> (24 + 2 * i)) & 3) != 0);
       for (int t = 0; t < n_ent && ok; ++t) {
-        const int e = entries[t];
-        const int en = (t + 1 < n_ent) ? entries[t + 1] : 0;
-        for (int i = 0; i < 2 && ok; ++i) {
-          if ((e >> (24 + 2 * i)) & 3) ok = issue_pv(i, t);
-          if (ok && t + 1 < n_ent && ((en >> (24 + 2 * i)) & 3)) ok = issue_s(i, t + 1);
-        }
-        if (!ok) break;
-        if (t + 1 < n_ent) tc_commit(bar_kv_empty + (2 * (t + 1)) % NS);
-        tc_commit(bar_kv_empty + (2 * t + 1) % NS);
+        ok = issue_pv(t, ((entries[t] >> (24 + 2 * i)) & 3) != 0);
+        if (ok && t + 1 < n_ent) ok = issue_s(t + 1, ((entries[t + 1] >> (24 + 2 * i)) & 3) != 0);
       }
       if (!ok) {
         report_status(a.status, FA_ERR_TIMEOUT);
         *abort_flag = 1;
       }
-      // Teardown: wait (bounded) until every MMA issued above has retired.
-      tc_commit(bar_teardown);
+      // Teardown: wait (bounded) until every MMA this thread issued has retired.
+      tc_commit(bar_teardown + i);
       volatile int never = 0;
-      mbar_wait(bar_teardown, 0, &never);
+      mbar_wait(bar_teardown + i, 0, &never);
     }
     __syncwarp();
+  }
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ---------------------------------------------------------------- softmax (thread = row)
     const int i = warp >> 2;
     const int wq = warp & 3;
@@ -282,15 +323,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tO = t_lane + TM_O0 + D * i;
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
-    const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && q_row < a.Tq ? __ldg(mc.doc_q + q_row) : 0;
+    const int qg = q_row + mc.q_off;  // global position of this row (mask and score mods)
+    const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && q_row < a.Tq ? __ldg(mc.doc_q + qg) : 0;
     // Causal, window and the Tkv bound intersect to one allowed kv interval [row_lo, row_hi]
     // per row; partial tiles test it with two compares.  Document and tile-table predicates
     // (if enabled) are evaluated per element on top.
-    int row_lo = 0, row_hi = a.Tkv - 1;
-    if (mc.flags & FA_MASK_CAUSAL) row_hi = min(row_hi, q_row);
+    int row_lo = mc.kv_off, row_hi = mc.Tkv - 1;  // global kv positions
+    if (mc.flags & FA_MASK_CAUSAL) row_hi = min(row_hi, qg);
     if (mc.flags & FA_MASK_WINDOW) {
-      if (mc.left >= 0) row_lo = max(row_lo, q_row - mc.left);
-      if (mc.right >= 0) row_hi = min(row_hi, q_row + mc.right);
+      if (mc.left >= 0) row_lo = max(row_lo, qg - mc.left);
+      if (mc.right >= 0) row_hi = min(row_hi, qg + mc.right);
     }
     const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
 
@@ -301,8 +343,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int t = 0; t < n_ent; ++t) {
       const int e = entries[t];
       const int code = (e >> (24 + 2 * i)) & 3;
-      if (!code) continue;
-      const int kv0 = (e & 0xFFFFFF) * kBN;
+      // Ping-pong (when enabled): the two softmax warpgroups take strict turns (0, 1, 0, 1, ...),
+      // one turn per kv entry each, visited or not, so one warpgroup's exponentials run while
+      // the tensor cores work on the other sub-tile's PV and next S.  Turn k of warpgroup 0
+      // needs warpgroup 1's (k-1)-th hand-over; turn k of warpgroup 1 needs warpgroup 0's k-th.
+      if (pingpong) {
+        if (!mbar_wait(bar_turn + i, i == 0 ? ((t & 1) ^ 1) : (t & 1), abort_flag)) { ok = false; break; }
+        if (!code) {
+          mbar_arrive(bar_turn + (1 - i));
+          continue;
+        }
+      } else if (!code) {
+        continue;
+      }
+      const int kvg0 = (e & 0xFFFFFF) * kBN + mc.kv_off;  // global position of the tile's first key
       if (!mbar_wait(bar_s_full + i, s_phase, abort_flag)) { ok = false; break; }
       s_phase ^= 1;
       tc_fence_after();
@@ -327,18 +381,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // scale is positive) and the scale folds into the exponent's FFMA.
       if constexpr (SK != SC_NONE) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], q_row, kv0 + c, sc);
+        for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], qg, kvg0 + c, sc);
       }
       if (code & 1) {
         const unsigned span = (unsigned)(row_hi - row_lo);
-        const int clo = row_lo - kv0;
+        const int clo = row_lo - kvg0;
 #pragma unroll
         for (int c = 0; c < kBN; ++c)
           if ((unsigned)(c - clo) > span || row_hi < row_lo) x[c] = -INFINITY;
         if (per_elem_mask) {
 #pragma unroll
           for (int c = 0; c < kBN; ++c)
-            if (!mask_ok(mc, q_row, kv0 + c, dq_val)) x[c] = -INFINITY;
+            if (!mask_ok(mc, qg, kvg0 + c, dq_val)) x[c] = -INFINITY;
         }
       }
       float m8[8];
@@ -360,15 +414,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float2 nm2 = make_float2(-m_use, -m_use);
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
+      // Full tiles hold no -inf, so some exponentials may take the polynomial path.
+      const bool emu = (code & 1) == 0;
 #pragma unroll
       for (int c0 = 0; c0 < kBN; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           const float2 y = __ffma2_rn(make_float2(x[c0 + c], x[c0 + c + 1]), kk2, nm2);
-          const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+          float2 p;
+          if (((c >> 1) & 3) < FA_FWD_EXP_EMU && emu) p = exp2_poly2(y);
+          else p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
           sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
+#if FA_FWD_INT_PACK
+          pk[c >> 1] = pack_bf16x2_int(p.x, p.y);
+#else
           pk[c >> 1] = pack_bf16x2(p.x, p.y);
+#endif
         }
         tmem_st16(tS + (c0 >> 1), pk);
       }
@@ -391,6 +453,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar_p_full + i);
+      if (pingpong) mbar_arrive(bar_turn + (1 - i));
       ++processed;
     }
     if (!ok) {
@@ -449,7 +512,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
 int fwd_tc_max_stages(int D, int nkv) {
   int best = 0;
-  for (int ns = 2; ns <= 8; ++ns)
+  for (int ns = 2; ns <= 12; ++ns)
     if (fwd_smem_layout(D, ns, nkv).total <= 227 * 1024) best = ns;
   return best;
 }
@@ -460,10 +523,23 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   const int npairs = (a.bt.nq + 1) / 2;
   const dim3 grid((unsigned)(npairs * a.B * a.H));
   const int sk = score_kind_of(a.score.flags);
+  // Strict softmax turns pay off when the tensor cores bound the loop (head dim 128, no
+  // score_mod, no per-element mask predicate); a heavier softmax runs better with both
+  // warpgroups in flight at once.
+#if FA_FWD_PINGPONG < 0
+  const int pingpong = a.D == 128 && sk == SC_NONE && !(a.mask.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE));
+#else
+  const int pingpong = FA_FWD_PINGPONG;
+#endif
   auto go = [&](auto kern) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.
+    cudaFuncAttributes fa_attr;
+    cudaError_t e = cudaFuncGetAttributes(&fa_attr, kern);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a);
+    if (fa_attr.numRegs * kFwdThreads < 2 * 128 * kRegsSoftmax + 128 * kRegsCtl) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a, pingpong);
     return cudaGetLastError();
   };
 #define FA_FWD_CASE(DD, SKK) \

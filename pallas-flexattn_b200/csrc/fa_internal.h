@@ -15,7 +15,7 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
 // tcgen05 backward (fa_bwd_sm100.cu)
 int bwd_tc_max_stages(int D, int nq);
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          const CUtensorMap& tdo, cudaStream_t stream);
+                          const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream);
 
 // generic CUDA-core kernels (fa_simt.cu)
 cudaError_t launch_fwd_simt(const AttnArgs& a, int dtype, cudaStream_t stream);

@@ -85,6 +85,23 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Tiled bulk reduce-add shared -> global (element type from the tensor map), tracked
+// by the issuing thread's bulk group.  Coordinates are non-negative; x is a multiple
+// of 16 bytes.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the source buffers of this thread's committed bulk groups have been read.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until this thread's committed bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -131,6 +148,32 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same two MMAs with the 64-bit descriptors passed as (lo, hi) halves.  An issuer
+// that precomputes a tile's base descriptor advances it per K step with one 32-bit
+// add on `lo` (the 14-bit start-address field never carries: shared addresses are
+// < 256 KB), keeping the issue loop to a few instructions per MMA.
+__device__ __forceinline__ void mma_ss_lh(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                          uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -203,6 +246,18 @@ __device__ __forceinline__ void reg_pin(uint32_t (&r)[N]) {
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
+// ---------------------------------------------------------------- register rebalancing
+// Executed by every warp of a warpgroup.  The host checks before launch that the
+// per-warpgroup targets sum to no more than the block's launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -214,6 +269,38 @@ __device__ __forceinline__ float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x on the FMA pipes for a pair of inputs (Cody-Waite split x = j + f, j = round(x),
+// f in [-1/2, 1/2]; 2^f from a cubic fitted here to minimise the relative error on that
+// interval: max 7.6e-5, far below bf16's 2^-9).  Inputs are clamped to >= -126, so the
+// result is >= 0 and tiny for very negative x; it is NOT 0 for x = -inf, so callers use it
+// only where no element is masked.  Offloads the MUFU pipe (the split-exponential idea
+// published with FlashAttention-4).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  const float2 lo = make_float2(-126.f, -126.f);
+  x = make_float2(fmaxf(x.x, lo.x), fmaxf(x.y, lo.y));
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const float2 t = __fadd2_rn(x, magic);                    // round(x) in the low mantissa bits
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __fadd2_rn(x, make_float2(-j.x, -j.y));
+  float2 p = __ffma2_rn(make_float2(0.05516812205314636f, 0.05516812205314636f), f,
+                        make_float2(0.24260260164737701f, 0.24260260164737701f));
+  p = __ffma2_rn(p, f, make_float2(0.6932608485221863f, 0.6932608485221863f));
+  p = __ffma2_rn(p, f, make_float2(0.9999287128448486f, 0.9999287128448486f));
+  // scale by 2^j: add j to the exponent field (the magic constant's bits vanish in the shift)
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// bf16x2 packing on the integer pipes for non-negative finite inputs (probabilities):
+// add half a unit of the dropped 16 bits (round half up; differs from round-to-nearest-
+// even only on exact ties) and keep the high halves with one byte permute.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   // cvt packs its first source into the upper half.

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_simt_kernel(const AttnArgs a)
 
   const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
   const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
-  const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && row_ok ? mc.doc_q[q_row] : 0;
+  const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && row_ok ? mc.doc_q[q_row + mc.q_off] : 0;
 
   if (row_ok) {
     const T* q = row_ptr<T>(a.q, b, h, q_row);
@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(kWarps * 32) fwd_simt_kernel(const AttnArgs a)
       const int kv = c0 + lane;
       float dot = 0.f;
       for (int d = 0; d < D; ++d) dot = fmaf(sQ[warp * D + d], sK[lane * DP + d], dot);
-      float x = score_nat(dot, q_row, kv, sc, nullptr);
-      if (kv >= t_end || (partial && !mask_ok(mc, q_row, kv, dq_val))) x = -INFINITY;
+      float x = score_nat(dot, q_row + mc.q_off, kv + mc.kv_off, sc, nullptr);
+      if (kv >= t_end || (partial && !mask_ok(mc, q_row + mc.q_off, kv + mc.kv_off, dq_val))) x = -INFINITY;
       const float m_new = fmaxf(m, warp_max(x));
       const float alpha = (m_new == -INFINITY) ? 1.f : expf(m - m_new);
       const float p = (m_new == -INFINITY) ? 0.f : expf(x - m_new);
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dq_simt_kernel(const AttnArgs
 
   const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
   const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
-  const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && row_ok ? mc.doc_q[q_row] : 0;
+  const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && row_ok ? mc.doc_q[q_row + mc.q_off] : 0;
   float lse = -INFINITY, delta = 0.f;
   if (row_ok) {
     const T* q = row_ptr<T>(a.q, b, h, q_row);
@@ -252,8 +252,8 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dq_simt_kernel(const AttnArgs
         dp = fmaf(sdO[warp * D + d], sV[lane * DP + d], dp);
       }
       float g;
-      const float x = score_nat(dot, q_row, kv, sc, &g);
-      const bool live = kv < t_end && !(partial && !mask_ok(mc, q_row, kv, dq_val)) && lse != -INFINITY;
+      const float x = score_nat(dot, q_row + mc.q_off, kv + mc.kv_off, sc, &g);
+      const bool live = kv < t_end && !(partial && !mask_ok(mc, q_row + mc.q_off, kv + mc.kv_off, dq_val)) && lse != -INFINITY;
       const float p = live ? expf(x - lse) : 0.f;
       const float ds = p * (dp - delta) * g;
       for (int jj = 0; jj < kChunk; ++jj) {
@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dkv_simt_kernel(const AttnArg
         const int q = c0 + r;
         sL[r] = q < t_end ? a.lse_in[(int64_t)bh * a.Tq + q] : -INFINITY;
         sDl[r] = q < t_end ? a.delta[(int64_t)bh * a.Tq_pad + q] : 0.f;
-        sDoc[r] = (q < t_end && (mc.flags & FA_MASK_DOCUMENT)) ? mc.doc_q[q] : 0;
+        sDoc[r] = (q < t_end && (mc.flags & FA_MASK_DOCUMENT)) ? mc.doc_q[q + mc.q_off] : 0;
       }
       __syncthreads();
       if (!row_ok) continue;
@@ -347,9 +347,9 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dkv_simt_kernel(const AttnArg
         dp = fmaf(sdO[lane * DP + d], sV[warp * D + d], dp);
       }
       float g;
-      const float x = score_nat(dot, q, kv_row, sc, &g);
+      const float x = score_nat(dot, q + mc.q_off, kv_row + mc.kv_off, sc, &g);
       const float lse = sL[lane];
-      const bool live = q < t_end && !(partial && !mask_ok(mc, q, kv_row, sDoc[lane])) && lse != -INFINITY;
+      const bool live = q < t_end && !(partial && !mask_ok(mc, q + mc.q_off, kv_row + mc.kv_off, sDoc[lane])) && lse != -INFINITY;
       const float p = live ? expf(x - lse) : 0.f;
       const float ds = p * (dp - sDl[lane]) * g;
       for (int jj = 0; jj < kChunk; ++jj) {

@@ -33,6 +33,8 @@ class FaMaskSpec(C.Structure):
         ("table_rows", C.c_int32),
         ("table_cols", C.c_int32),
         ("table_block", C.c_int32),
+        ("q_offset", C.c_int32),
+        ("kv_offset", C.c_int32),
     ]
 
 
@@ -43,6 +45,7 @@ class FaScoreSpec(C.Structure):
         ("alibi_slopes", C.c_void_p),
         ("rel_bias", C.c_void_p),
         ("rel_bias_stride_h", C.c_int64),
+        ("rel_bias_center", C.c_int32),
     ]
 
 

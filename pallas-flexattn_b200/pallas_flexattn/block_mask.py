@@ -92,13 +92,14 @@ def _stream(device) -> int:
 
 
 def build_tables_from_spec(spec: MaskSpec, B: int, Tq: int, Tkv: int, block_q: int, block_kv: int,
-                           device, mode: int = L.FA_BLOCK_MASK_EXACT) -> BlockTables:
-    """Classify every tile of the mask on the GPU and build all tables."""
+                           device, mode: int = L.FA_BLOCK_MASK_EXACT, offsets: tuple = (0, 0)) -> BlockTables:
+    """Classify every tile of the mask on the GPU and build all tables.  `offsets` are the
+    global positions of the first query and key (a block of a longer sequence)."""
     device = torch.device(device)
     nq, nkv = math.ceil(Tq / block_q), math.ceil(Tkv / block_kv)
     num_b = B if spec.depends_on_batch else 1
     bt, out = _alloc_tables(num_b, nq, nkv, block_q, block_kv, device)
-    m = spec.to_c(device, Tq, Tkv)
+    m = spec.to_c(device, Tq, Tkv, *offsets)
     with torch.cuda.device(device):
         L.check(L.lib().fa_create_block_mask(C.byref(m), B, Tq, Tkv, block_q, block_kv, mode, C.byref(out),
                                              _stream(device)))

@@ -77,11 +77,12 @@ def clear_table_cache() -> None:
     _TABLE_CACHE.clear()
 
 
-def _tables_for(spec: MaskSpec, B: int, Tq: int, Tkv: int, bq: int, bkv: int, device) -> BlockTables:
-    key = (spec.key(), B if spec.depends_on_batch else 1, Tq, Tkv, bq, bkv, str(device))
+def _tables_for(spec: MaskSpec, B: int, Tq: int, Tkv: int, bq: int, bkv: int, device,
+                offsets: tuple = (0, 0)) -> BlockTables:
+    key = (spec.key(), B if spec.depends_on_batch else 1, Tq, Tkv, bq, bkv, str(device), tuple(offsets))
     bt = _TABLE_CACHE.get(key)
     if bt is None:
-        bt = build_tables_from_spec(spec, B, Tq, Tkv, bq, bkv, device)
+        bt = build_tables_from_spec(spec, B, Tq, Tkv, bq, bkv, device, offsets=offsets)
         _TABLE_CACHE[key] = bt
         while len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
             _TABLE_CACHE.popitem(last=False)
@@ -112,7 +113,8 @@ def _tc_ok_tensor(t: torch.Tensor) -> bool:
 class _Plan:
     """Everything one forward/backward call needs: resolved specs, tables, kernel choice."""
 
-    def __init__(self, q, k, v, mask_mod, score_mod, block_mask, block_r, block_c, num_stages, scale, need_bwd):
+    def __init__(self, q, k, v, mask_mod, score_mod, block_mask, block_r, block_c, num_stages, scale, need_bwd,
+                 offsets: tuple = (0, 0)):
         if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
             raise ValueError("q, k, v must be (B, H, T, D)")
         if not (q.is_cuda and k.is_cuda and v.is_cuda):
@@ -155,7 +157,7 @@ class _Plan:
             tc = tc and bt.block_q == TC_TILE and bt.block_kv == TC_TILE
         else:
             bq, bkv = (TC_TILE, TC_TILE) if tc else (int(block_r), int(block_c))
-            bt = _tables_for(mspec, B, Tq, Tkv, bq, bkv, self.device)
+            bt = _tables_for(mspec, B, Tq, Tkv, bq, bkv, self.device, offsets)
         if bt.nq != math.ceil(Tq / bt.block_q) or bt.nkv != math.ceil(Tkv / bt.block_kv):
             raise ValueError(f"block mask for ({bt.nq} x {bt.nkv}) tiles does not match Tq={Tq}, Tkv={Tkv}")
         if bt.num_b not in (1, B):
@@ -165,7 +167,7 @@ class _Plan:
         self.tc = tc
         self.kernel = L.FA_KERNEL_AUTO if tc else L.FA_KERNEL_SIMT
         self.num_stages = int(num_stages) if num_stages else 0
-        self.c_mask = mspec.to_c(self.device, Tq, Tkv)
+        self.c_mask = mspec.to_c(self.device, Tq, Tkv, *offsets)
         self.c_score = sspec.to_c(self.device, H, Tq, Tkv)
         self.c_tables = bt.to_c()
         self.status = device_status(self.device)

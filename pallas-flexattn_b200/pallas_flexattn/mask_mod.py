@@ -64,17 +64,19 @@ class MaskSpec:
             self._dev[k] = d
         return self._dev[k]
 
-    def to_c(self, device: torch.device, Tq: int, Tkv: int) -> L.FaMaskSpec:
+    def to_c(self, device: torch.device, Tq: int, Tkv: int, q_offset: int = 0, kv_offset: int = 0) -> L.FaMaskSpec:
         m = L.FaMaskSpec()
         m.flags = self.flags
         m.window_left = self.window_left
         m.window_right = self.window_right
+        m.q_offset, m.kv_offset = int(q_offset), int(kv_offset)
         dev = self.device_tensors(device)
         if self.flags & L.FA_MASK_DOCUMENT:
             doc = dev["doc"]
             T = doc.shape[-1]
-            if T < max(Tq, Tkv):
-                raise ValueError(f"document ids cover {T} positions, attention needs {max(Tq, Tkv)}")
+            if T < max(q_offset + Tq, kv_offset + Tkv):
+                raise ValueError(f"document ids cover {T} positions, attention needs "
+                                 f"{max(q_offset + Tq, kv_offset + Tkv)}")
             m.doc_q = doc.data_ptr()
             m.doc_kv = doc.data_ptr()
             m.doc_stride_b = T if (doc.dim() == 2 and doc.shape[0] > 1) else 0
