@@ -67,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 4-D tiled load (no multicast).  x is the innermost (head-dim) coordinate; callers
+// 4-D tiled load into this CTA's shared memory.  x is the innermost (head-dim) coordinate; callers
 // keep it a multiple of 64 elements, so it is always 16-byte aligned.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             int z, int w) {
