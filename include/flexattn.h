@@ -176,6 +176,20 @@ FA_API int fa_bwd_workspace_size(const FaBwdParams* p, size_t* bytes);
  * dK/dV/dQ kernel and the dQ conversion. */
 FA_API int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_stream_t stream);
 
+/* Backward like fa_bwd, but allocation-free: the workspace is a static device array of
+ * FA_NOALLOC_SCRATCH_BYTES inside the library instead of caller memory.  No counterpart
+ * in the reference (its backward gets scratch from the XLA runtime); it serves hosts that
+ * hold device pointers but no device allocator, e.g. a cgo/JNI/ctypes binding running
+ * inside another runtime's memory pool, where a cudaMalloc bypasses the pool and can
+ * fail once the pool has reserved most of the HBM.
+ * - Limit: a shape whose fa_bwd_workspace_size exceeds FA_NOALLOC_SCRATCH_BYTES returns
+ *   FA_ERR_UNSUPPORTED before anything runs (use fa_bwd for it).
+ * - The first call on each device, with that device current, resolves the scratch address
+ *   and loads the kernels; make it before any stream capture.
+ * - Calls that overlap on one device share the scratch and race: serialise them. */
+#define FA_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+FA_API int fa_bwd_noalloc(const FaBwdParams* p, fa_stream_t stream);
+
 /* Block-mask construction on the GPU. */
 enum {
   FA_BLOCK_MASK_EXACT = 0, /* tile listed iff any element is unmasked; "full" iff all are */

@@ -131,6 +131,10 @@ AttnArgs base_args(int B, int H, int Hkv, int Tq, int Tkv, int D, float scale, c
 }
 
 }  // namespace
+
+// Sets the thread's fa_last_error message from another translation unit; returns `code`.
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace fa
 
 using namespace fa;

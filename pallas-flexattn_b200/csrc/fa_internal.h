@@ -7,6 +7,8 @@
 
 namespace fa {
 
+int set_last_error(int code, const char* msg);
+
 // tcgen05 forward (fa_fwd_sm100.cu)
 int fwd_tc_max_stages(int D, int nkv);
 cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,

@@ -17,6 +17,7 @@ FA_KERNEL_AUTO, FA_KERNEL_TC, FA_KERNEL_SIMT = 0, 1, 2
 FA_MASK_CAUSAL, FA_MASK_WINDOW, FA_MASK_DOCUMENT, FA_MASK_TILE_TABLE = 1, 2, 4, 8
 FA_SCORE_ALIBI, FA_SCORE_SOFTCAP, FA_SCORE_REL_BIAS = 1, 2, 4
 FA_BLOCK_MASK_EXACT, FA_BLOCK_MASK_REF9 = 0, 1
+FA_NOALLOC_SCRATCH_BYTES = 64 << 20  # static scratch of fa_bwd_noalloc
 
 _i32p = C.POINTER(C.c_int32)
 
@@ -156,6 +157,7 @@ EXPORTS = {
     "fa_bwd_preprocess": (C.c_int, [C.POINTER(FaBwdParams), C.c_void_p, C.c_void_p, C.c_void_p]),
     "fa_bwd_workspace_size": (C.c_int, [C.POINTER(FaBwdParams), C.POINTER(C.c_size_t)]),
     "fa_bwd": (C.c_int, [C.POINTER(FaBwdParams), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "fa_bwd_noalloc": (C.c_int, [C.POINTER(FaBwdParams), C.c_void_p]),
     "fa_create_block_mask": (
         C.c_int,
         [C.POINTER(FaMaskSpec), C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,

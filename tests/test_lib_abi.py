@@ -44,6 +44,10 @@ def test_error_path_without_gpu():
     bp.B, bp.H, bp.Tq, bp.D = 2, 3, 5, 64
     assert L.lib().fa_bwd_workspace_size(C.byref(bp), C.byref(size)) == 0
     assert size.value >= 2 * 3 * 5 * 4 + 2 * 3 * 5 * 64 * 4
+    # the no-alloc backward turns away a shape beyond its static scratch before any CUDA call
+    bp.B, bp.H, bp.H_kv, bp.Tq, bp.Tkv, bp.D = 1, 16, 16, 8192, 8192, 128
+    assert L.lib().fa_bwd_noalloc(C.byref(bp), None) == L.FA_ERR_UNSUPPORTED
+    assert b"static scratch" in L.lib().fa_last_error()
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
@@ -54,6 +58,7 @@ def test_ctypes_layout_matches_header(tmp_path):
         lines.append(f'printf("{s} size %zu\\n", sizeof({s}));')
         for f, _ in cls._fields_:
             lines.append(f'printf("{s}.{f} %zu\\n", offsetof({s}, {f}));')
+    lines.append('printf("FA_NOALLOC_SCRATCH_BYTES %zu\\n", FA_NOALLOC_SCRATCH_BYTES);')
     lines += ["return 0;", "}"]
     src = tmp_path / "probe.c"
     src.write_text("\n".join(lines))
@@ -61,6 +66,7 @@ def test_ctypes_layout_matches_header(tmp_path):
     subprocess.run(["gcc", "-std=c11", f"-I{REPO / 'include'}", str(src), "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
     got = dict(line.rsplit(" ", 1) for line in out if line)
+    assert int(got["FA_NOALLOC_SCRATCH_BYTES"]) == L.FA_NOALLOC_SCRATCH_BYTES
     for s in STRUCTS:
         cls = getattr(L, s)
         assert int(got[f"{s} size"]) == C.sizeof(cls), s
