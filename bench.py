@@ -15,8 +15,8 @@ Extra keys: ``roofline`` for the dominant kernel (algorithmic FLOPs per launch
 over its CUDA-event duration, against the measured bf16 peak), ``cpu_baseline``
 (the reference's tiled CPU path restated in torch, on one (b, h) slice),
 ``e2e`` (same step through the public API with pinned-host inputs copied in and
-a result row copied out each step), ``clocks`` (nvidia-smi sampled during the
-timed region) and ``gpu_launches``.
+a result row copied out each step), ``clocks`` (NVML sampled every 10 ms during
+the timed region) and ``gpu_launches``.
 
 ``--impl reference`` times the reference's CPU implementation of the path (the
 restatement in oracle/cpu_reference.py; the reference itself needs jax, which
@@ -57,60 +57,103 @@ def load_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed region runs.
+
+    Reads NVML (nvidia_ml_py) every 10 ms from a thread, so even a sub-second timed region
+    gets samples; falls back to `nvidia-smi -lms 100` when NVML cannot be opened.  Only
+    reads state: it never changes a clock or any other GPU setting.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    def __init__(self, device):
+        self.device = device
+        self.sm: list[float] = []
+        self.max_mhz = None
+        self.reasons: set = set()
         self.lines: list[str] = []
+        self.proc = None
         self.thread = None
+        self.stop = threading.Event()
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml as N
+        N.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            return N, N.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:
+            return N, N.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+
+    def _poll_nvml(self, N, h):
+        bits = {"hw_slowdown": N.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": N.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": N.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": N.nvmlClocksEventReasonSwPowerCap}
+        while not self.stop.is_set():
+            try:
+                self.sm.append(float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)))
+                r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.reasons.update(n for n, b in bits.items() if r & b)
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __enter__(self):
         try:
+            N, h = self._nvml_handle()
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            self.nvml = N
+            self.thread = threading.Thread(target=self._poll_nvml, args=(N, h), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+                ["nvidia-smi", f"--id=GPU-{torch.cuda.get_device_properties(self.device).uuid}",
+                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
         except (OSError, ValueError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            if self.thread:
-                self.thread.join(timeout=2)
-
-    def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        if self.thread:
+            self.thread.join(timeout=2)
+        for ln in self.lines:  # nvidia-smi fallback
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                self.sm.append(float(parts[1]))
+                self.max_mhz = float(parts[2])
             except ValueError:
                 continue
-            for n, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            self.reasons.update(n for n, flag in zip(self.NAMES, parts[5:9]) if flag.lower() == "active")
+
+    def summary(self) -> dict:
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm),
+                "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 def dist_setup():
@@ -202,7 +245,7 @@ def run_reference(args, w, n_pairs, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", default="flexattn", choices=["flexattn", "reference"])
@@ -265,7 +308,7 @@ def main():
         barrier(dist)
         return s.elapsed_time(e) / n
 
-    with ClockSampler(device.index) as clk:
+    with ClockSampler(device) as clk:
         ms_step = timed(step, args.steps)
     ms_step = max_over_ranks(dist, ms_step, device)
     ms_fwd = max_over_ranks(dist, timed(fwd_only, args.steps), device)
