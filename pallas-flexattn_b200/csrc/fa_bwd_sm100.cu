@@ -16,7 +16,7 @@
 //   WG2 (warps 8-11)      dQ drain: thread = q row; TMEM -> swizzled smem -> TMA reduce-add
 //   WG3 (warps 12-15)     warp 12 TMA producer, warp 13 MMA issuer + TMEM owner, 14-15 idle
 // Registers: launched at 128 per thread (512 x 128 = 65536); setmaxnreg moves them to
-// 176 for WG0/WG1, 96 for WG2, 64 for WG3 (2*128*176 + 128*96 + 128*64 = 65536).
+// 176 for WG0/WG1, 80 for WG2, 80 for WG3 (2*128*176 + 128*80 + 128*80 = 65536).
 // TMEM columns: St [0,128) (Pt bf16 written back into its own half), dPt [128,256)
 // (reused for dQ_i once dSt is in shared memory), dV [256,256+D), dK [256+D,256+2D).
 // dSt is stored once in shared memory in the 128-byte-swizzled K-major layout; the
@@ -37,7 +37,7 @@ constexpr int kBM = 128;  // kv rows per CTA
 constexpr int kBQ = 128;  // q rows per iteration
 constexpr int kBwdThreads = 512;
 constexpr int kWarpDq0 = 8, kWarpProd = 12, kWarpMma = 13;
-constexpr int kRegsCompute = 176, kRegsDrain = 96, kRegsCtl = 64;
+constexpr int kRegsCompute = 176, kRegsDrain = 80, kRegsCtl = 80;
 constexpr int kChunk = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row bf16 tile
 constexpr int kDqStage = 32 * 32 * 4;  // per drain warp: 32 rows x 32 fp32, 128B-swizzled
 
@@ -284,15 +284,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           // dK += dSt Q ; dQ_i = dS K
           if (!(ok = mbar_wait(bar_ds_full, ph, abort_flag))) break;
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kBQ / 16; ++kk)
-            mma_ss_lh(tmem_base + TM_DK, S_k + kofs(kk), hi, Q_mn + mofs(kk), hi, IDESC_KV, kk > 0 ? 1u : acc0);
+          // dQ first: the drain (and, through it, the next dPt) waits on it; dK runs meanwhile.
 #pragma unroll
           for (int kk = 0; kk < kBM / 16; ++kk)
             mma_ss_lh(tmem_base + TM_DP, S_mn + mofs(kk), hi, K_mn + mofs(kk), hi, IDESC_DQ, kk > 0);
+          tc_commit(bar_dq_full);
+#pragma unroll
+          for (int kk = 0; kk < kBQ / 16; ++kk)
+            mma_ss_lh(tmem_base + TM_DK, S_k + kofs(kk), hi, Q_mn + mofs(kk), hi, IDESC_KV, kk > 0 ? 1u : acc0);
           tc_commit(bar_q_empty + qs);
           tc_commit(bar_ds_empty);
-          tc_commit(bar_dq_full);
         }
         if (ok) tc_commit(bar_dkv_full);
         if (!ok) {
@@ -357,6 +358,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
     const int kvg = kv + mc.kv_off;
+    const float inv_cap_log2 = sc.inv_cap * kLn2;  // 1 / (cap * log2(e))
+    // Causal, window and the Tq/Tkv bounds intersect to one allowed q interval [q_lo, q_hi]
+    // (global positions) for this thread's kv row; partial tiles test it with two compares.
+    // Document and tile-table predicates, when enabled, are evaluated per element on top.
+    int q_lo = mc.q_off, q_hi = mc.q_off + a.Tq - 1;
+    if (kvg >= mc.Tkv) q_hi = q_lo - 1;
+    if (mc.flags & FA_MASK_CAUSAL) q_lo = max(q_lo, kvg);
+    if (mc.flags & FA_MASK_WINDOW) {
+      if (mc.left >= 0) q_hi = min(q_hi, kvg + mc.left);
+      if (mc.right >= 0) q_lo = max(q_lo, kvg - mc.right);
+    }
+    const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];
@@ -370,38 +383,44 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
       if (!(ok = mbar_wait(bar_s_full, ph, abort_flag))) break;
       tc_fence_after();
+      // p stays fp32 until dSt is formed; each 32-column half of Pt goes back to TMEM (bf16,
+      // into already-read S columns) as soon as it is computed, to keep registers low.
       float p[64];
-      uint32_t g2[(SK == SC_SOFTCAP || SK == SC_GENERAL) ? 32 : 1];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t s[32];
         tmem_ld32(t_lane + TM_S + cbase + 32 * hh, s);
+        float l2[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 v4 = reinterpret_cast<const float4*>(lse2 + 32 * hh)[u];
+          l2[4 * u] = v4.x; l2[4 * u + 1] = v4.y; l2[4 * u + 2] = v4.z; l2[4 * u + 3] = v4.w;
+        }
         tmem_ld_wait();
         reg_pin(s);
+        const int qg0 = q0 + 32 * hh + mc.q_off;  // global position of column 0 of this half
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int cc = 32 * hh + c;
-          const int q = q0 + cc;            // local row
-          const int qg = q + mc.q_off;      // global positions for the mask and score mods
-          const float x = score_log2<SK>(__uint_as_float(s[c]), qg, kvg, sc);
-          float pv = ex2_approx(x - lse2[cc]);
-          if (partial) {
-            const int dq = (mc.flags & FA_MASK_DOCUMENT) && q < a.Tq ? __ldg(mc.doc_q + qg) : 0;
-            if (!mask_ok(mc, qg, kvg, dq)) pv = 0.f;
-          }
-          p[cc] = pv;
-          if constexpr (SK == SC_SOFTCAP || SK == SC_GENERAL) {
-            const float gv = score_grad<SK>(x, sc);
-            if (cc & 1) g2[cc >> 1] = pack_bf16x2(__uint_as_float(g2[cc >> 1]), gv);
-            else g2[cc >> 1] = __float_as_uint(gv);
+        for (int c = 0; c < 32; ++c)
+          p[32 * hh + c] = ex2_approx(score_log2<SK>(__uint_as_float(s[c]), qg0 + c, kvg, sc) - l2[c]);
+        if (partial) {
+          const unsigned span = (unsigned)(q_hi - q_lo);
+          const int clo = q_lo - qg0;
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if ((unsigned)(c - clo) > span || q_hi < q_lo) p[32 * hh + c] = 0.f;
+          if (per_elem_mask) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int q = qg0 - mc.q_off + c;  // local row
+              const int dq = (mc.flags & FA_MASK_DOCUMENT) && q < a.Tq ? __ldg(mc.doc_q + qg0 + c) : 0;
+              if (!mask_ok(mc, qg0 + c, kvg, dq)) p[32 * hh + c] = 0.f;
+            }
           }
         }
-      }
-      {
-        uint32_t pk[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = pack_bf16x2(p[2 * c], p[2 * c + 1]);
-        tmem_st32(t_lane + TM_S + (wg ? 64 : 0), pk);
+        for (int c = 0; c < 16; ++c) pk[c] = pack_bf16x2(p[32 * hh + 2 * c], p[32 * hh + 2 * c + 1]);
+        tmem_st16(t_lane + TM_S + (wg ? 64 : 0) + 16 * hh, pk);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -415,18 +434,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t dp[32];
         tmem_ld32(t_lane + TM_DP + cbase + 32 * hh, dp);
+        float dl32[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 v4 = reinterpret_cast<const float4*>(dl + 32 * hh)[u];
+          dl32[4 * u] = v4.x; dl32[4 * u + 1] = v4.y; dl32[4 * u + 2] = v4.z; dl32[4 * u + 3] = v4.w;
+        }
         tmem_ld_wait();
         reg_pin(dp);
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           const int cc = 32 * hh + c;
-          float d0 = p[cc] * (__uint_as_float(dp[c]) - dl[cc]);
-          float d1 = p[cc + 1] * (__uint_as_float(dp[c + 1]) - dl[cc + 1]);
+          float d0 = p[cc] * (__uint_as_float(dp[c]) - dl32[c]);
+          float d1 = p[cc + 1] * (__uint_as_float(dp[c + 1]) - dl32[c + 1]);
           if constexpr (SK == SC_SOFTCAP || SK == SC_GENERAL) {
-            const __nv_bfloat162 gg = *reinterpret_cast<const __nv_bfloat162*>(&g2[cc >> 1]);
-            d0 *= __low2float(gg);
-            d1 *= __high2float(gg);
+            // Softcap derivative 1 - t^2, with t = x / cap_log2 recovered from p = 2^(x - lse2)
+            // instead of being held in registers since the P phase.  p = 0 means dS = 0.
+            if (sc.flags & FA_SCORE_SOFTCAP) {
+              const float x0 = lg2_approx(p[cc]) + lse2[cc], x1 = lg2_approx(p[cc + 1]) + lse2[cc + 1];
+              const float t0 = x0 * inv_cap_log2, t1 = x1 * inv_cap_log2;
+              d0 *= p[cc] > 0.f ? fmaf(-t0, t0, 1.f) : 1.f;
+              d1 *= p[cc + 1] > 0.f ? fmaf(-t1, t1, 1.f) : 1.f;
+            }
           }
           pk[c >> 1] = pack_bf16x2(d0, d1);
         }
