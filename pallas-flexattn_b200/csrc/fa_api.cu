@@ -44,13 +44,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 4-D map over a bf16 [B, heads, T, D] tensor; box = 64 columns x 128 rows, 128-byte swizzle.
-int make_bf16_map(CUtensorMap* map, const FaTensor& t, int B, int heads, int T, int D, const char* name) {
+// 4-D map over a bf16 [B, heads, T, D] tensor; box = 64 columns x box_rows rows, 128-byte swizzle.
+int make_bf16_map(CUtensorMap* map, const FaTensor& t, int B, int heads, int T, int D, const char* name,
+                  int box_rows = 128) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)heads, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)t.stride_t * 2, (cuuint64_t)t.stride_h * 2, (cuuint64_t)t.stride_b * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.ptr, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -209,11 +210,12 @@ static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 static int pad128(int t) { return (t + 127) / 128 * 128; }
 
-// Workspace: delta [B*H, Tq_pad] | lse2 [B*H, Tq_pad] | dq_accum [B*H, Tq, D], fp32.
+// Workspace: delta [B*H, Tq_pad] | lse2 [B*H, Tq_pad] | dq_accum [B*H, Tq, D], fp32 (sized
+// B*H*Tq_pad*D: the preprocess kernel zeroes it per padded row).
 int fa_bwd_workspace_size(const FaBwdParams* p, size_t* bytes) {
   if (!p || !bytes) return fail(FA_ERR_INVALID, "NULL argument");
   const size_t prow = (size_t)p->B * p->H * pad128(p->Tq);
-  const size_t rows = (size_t)p->B * p->H * p->Tq;
+  const size_t rows = prow;
   *bytes = 2 * round_up(prow * sizeof(float), 256) + round_up(rows * p->D * sizeof(float), 256);
   return FA_OK;
 }
@@ -269,10 +271,11 @@ int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_str
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
     CUtensorMap tq, tk, tv, tdo, tdq;
-    if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q")) ||
+    const int qrows = bwd_tc_q_rows(p->D);
+    if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q", qrows)) ||
         (rc = make_bf16_map(&tk, p->k, p->B, p->H, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H, p->Tkv, p->D, "v")) ||
-        (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout")) ||
+        (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout", qrows)) ||
         (rc = make_dq_accum_map(&tdq, a.dq_accum, p->B * p->H, p->Tq, p->D)))
       return rc;
     e = launch_bwd_tc(a, tq, tk, tv, tdo, tdq, (cudaStream_t)stream);

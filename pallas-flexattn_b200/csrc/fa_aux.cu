@@ -25,6 +25,13 @@ __device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
+// Zeroes D floats of the dQ accumulator per padded row, B*H*Tq_pad*D in all (the
+// [B*H, Tq, D] accumulator is the first B*H*Tq*D of them).
+__device__ __forceinline__ void zero_dq_row(const AttnArgs& a, int64_t prow, int lane) {
+  float4* z = reinterpret_cast<float4*>(a.dq_accum + prow * a.D);
+  for (int d4 = lane; d4 < a.D / 4; d4 += 32) z[d4] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 // One warp per row of the padded [B*H, Tq_pad] grid.  Rows past Tq get delta = 0
 // and lse2 = +inf (so exp2(x - lse2) = 0 there); rows with lse = -inf (no key)
 // also get lse2 = +inf.
@@ -41,6 +48,7 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const Attn
       a.delta[prow] = 0.f;
       if (a.lse2) a.lse2[prow] = INFINITY;
     }
+    zero_dq_row(a, prow, lane);
     return;
   }
   const int64_t row = (int64_t)bh * a.Tq + t;
@@ -72,8 +80,7 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const Attn
       a.lse2[prow] = (l == -INFINITY) ? INFINITY : l * kLog2e;
     }
   }
-  float4* z = reinterpret_cast<float4*>(a.dq_accum + row * a.D);
-  for (int d4 = lane; d4 < a.D / 4; d4 += 32) z[d4] = make_float4(0.f, 0.f, 0.f, 0.f);
+  zero_dq_row(a, prow, lane);
 }
 
 template <typename T>

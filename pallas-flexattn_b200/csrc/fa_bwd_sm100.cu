@@ -2,25 +2,33 @@
 //
 // Replaces the reference's two backward kernels (src/pallas_flexattn/flash_attn.py:
 // dK/dV :206-253 and dQ :313-356), which recompute S and P twice (7 tile GEMMs per
-// tile pair), with one KV-stationary kernel doing 5:
+// tile pair), with one KV-stationary kernel doing 5 per step:
 //   St  = K Q_i^T          dPt = V dO_i^T          (TMEM, fp32)
 //   Pt  = exp2(score(St) - lse2_i)   dSt = Pt * (dPt - delta_i) * score'   (registers)
 //   dV += Pt dO_i  (A = Pt from TMEM)   dK += dSt Q_i   dQ_i = dS K   (fp32 in TMEM)
-// dQ_i is added into an fp32 accumulator in global memory with TMA reduce-add by a
-// dedicated warpgroup; fa_bwd scales and converts it afterwards.  The CTA walks the
-// transposed block table (q_indices / full_q_indices) of its kv tile, skipping empty
-// tiles; full tiles do not evaluate the mask.
+// The CTA owns one 128-row kv tile and walks the q tiles of the transposed block table
+// (q_indices / full_q_indices) in steps of QR rows, skipping empty tiles; full tiles do
+// not evaluate the mask.
+//
+// A warpgroup drains dQ_i (TMEM -> swizzled shared stage -> TMA reduce-add into an fp32
+// accumulator in global memory; fa_bwd scales and converts it afterwards).  TMEM columns:
+//   D = 64:   S 128 | dP 128 | dQ 2 x 64 | dV 64 | dK 64   (dQ double-buffered: the drain has
+//             a whole step and never holds up the tensor cores)
+//   D = 128:  S 128 | dP 128 | dV 128 | dK 128             (full: dQ_i reuses the dP columns
+//             once dSt_i is formed, and dPt(t+1) waits for the drain of dQ_t)
+// Steps are 128 q rows for both, so every S / dP / dQ product is an N = 128 (or N = D) MMA:
+// narrower ones run below the tensor rate, bound by the shared-memory operand reads.
+//
+// MMA issue order: St(t) dPt(t) dV(t) St(t+1) dQ(t) dK(t) dPt(t+1) dV(t+1) ...  St(t+1)
+// goes out as soon as dV(t) has consumed Pt(t) from the S columns, so the next step's
+// exponentials can start the moment dSt(t) is written.
 //
 // Warp roles (512 threads, four warpgroups):
-//   WG0, WG1 (warps 0-7)  compute: thread = kv row; WG0 takes q columns 0-63, WG1 64-127
-//   WG2 (warps 8-11)      dQ drain: thread = q row; TMEM -> swizzled smem -> TMA reduce-add
+//   WG0, WG1 (warps 0-7)  compute: thread = kv row; WG0 takes q columns [0, QR/2), WG1 the rest
+//   WG2 (warps 8-11)      dQ drain: thread = TMEM lane (d for D = 128, q row for D = 64)
 //   WG3 (warps 12-15)     warp 12 TMA producer, warp 13 MMA issuer + TMEM owner, 14-15 idle
 // Registers: launched at 128 per thread (512 x 128 = 65536); setmaxnreg moves them to
-// 176 for WG0/WG1, 80 for WG2, 80 for WG3 (2*128*176 + 128*80 + 128*80 = 65536).
-// TMEM columns: St [0,128) (Pt bf16 written back into its own half), dPt [128,256)
-// (reused for dQ_i once dSt is in shared memory), dV [256,256+D), dK [256+D,256+2D).
-// dSt is stored once in shared memory in the 128-byte-swizzled K-major layout; the
-// dK MMA reads it as K-major (M = kv) and the dQ MMA as MN-major (M = q).
+// (D = 128) 168 for WG0/WG1, 96 for WG2, 80 for WG3, or (D = 64) 176 / 80 / 80.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -34,36 +42,50 @@ namespace fa {
 namespace {
 
 constexpr int kBM = 128;  // kv rows per CTA
-constexpr int kBQ = 128;  // q rows per iteration
 constexpr int kBwdThreads = 512;
 constexpr int kWarpDq0 = 8, kWarpProd = 12, kWarpMma = 13;
-constexpr int kRegsCompute = 176, kRegsDrain = 80, kRegsCtl = 80;
-constexpr int kChunk = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row bf16 tile
-constexpr int kDqStage = 32 * 32 * 4;  // per drain warp: 32 rows x 32 fp32, 128B-swizzled
+// Register split per warpgroup role (setmaxnreg); each sums to 65536 over 512 threads.
+template <int D> struct BwdRegs;
+template <> struct BwdRegs<128> { static constexpr int compute = 168, drain = 96, ctl = 80; };
+template <> struct BwdRegs<64> { static constexpr int compute = 176, drain = 80, ctl = 80; };
+constexpr int kDqStage = 32 * 32 * 4;  // 32 rows x 32 fp32, 128-byte swizzled; one per drain warp
+
+template <int D>
+struct BwdCfg {
+  static constexpr int QR = 128;                  // q rows per step
+  static constexpr int NP = QR / 2;               // q columns per compute thread
+  static constexpr bool DQ_OWN = D == 64;         // dQ has TMEM buffers of its own (two)
+  static constexpr int PANEL_K = kBM * 128;       // one 64-column swizzle panel of a K/V tile
+  static constexpr int PANEL_Q = QR * 128;        // of a Q/dO tile
+  static constexpr int PANEL_S = kBM * 128;       // of the dSt tile (rows = kv)
+  static constexpr uint32_t TM_S = 0, TM_DP = QR, TM_DQ = DQ_OWN ? 2 * QR : TM_DP,
+                            TM_DV = DQ_OWN ? 2 * QR + 2 * D : 2 * QR, TM_DK = TM_DV + D;
+  static_assert(TM_DK + D == 512, "TMEM plan must fill the 512 columns");
+};
 
 struct BwdSmemLayout {
-  int tile, nq_st, no_st, k_off, v_off, q_off, o_off, ds_off, dq_off, lse_off, dl_off, bar_off, misc_off, cls_off,
+  int ktile, qtile, k_off, v_off, q_off, o_off, ds_off, dq_off, lse_off, dl_off, bar_off, misc_off, cls_off,
       ent_off, total;
 };
 
 __host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int no_st, int nq) {
+  const int QR = 128;
   BwdSmemLayout L;
-  L.tile = kBM * D * 2;
-  L.nq_st = nq_st;
-  L.no_st = no_st;
+  L.ktile = kBM * D * 2;
+  L.qtile = QR * D * 2;
   L.k_off = 0;
-  L.v_off = L.tile;
-  L.q_off = 2 * L.tile;
-  L.o_off = L.q_off + nq_st * L.tile;
-  L.ds_off = L.o_off + no_st * L.tile;
-  L.dq_off = L.ds_off + kBQ * kBM * 2;
+  L.v_off = L.ktile;
+  L.q_off = 2 * L.ktile;
+  L.o_off = L.q_off + nq_st * L.qtile;
+  L.ds_off = L.o_off + no_st * L.qtile;
+  L.dq_off = L.ds_off + kBM * QR * 2;
   L.lse_off = L.dq_off + 4 * kDqStage;
-  L.dl_off = L.lse_off + nq_st * kBQ * 4;
-  L.bar_off = L.dl_off + nq_st * kBQ * 4;
-  L.misc_off = L.bar_off + (2 * nq_st + 2 * no_st + 12) * 8;
+  L.dl_off = L.lse_off + nq_st * QR * 4;
+  L.bar_off = L.dl_off + nq_st * QR * 4;
+  L.misc_off = L.bar_off + (2 * nq_st + 2 * no_st + 16) * 8;
   L.cls_off = L.misc_off + 16;
   L.ent_off = L.cls_off + 4 * nq;
-  L.total = L.ent_off + 4 * nq + 1024;
+  L.total = L.ent_off + 4 * 2 * nq + 1024;  // entries: up to two q steps per 128-row q block
   return L;
 }
 
@@ -72,11 +94,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                   const __grid_constant__ CUtensorMap tm_dq, const AttnArgs a, const int NQS, const int NOS) {
+  using C = BwdCfg<D>;
+  constexpr int QR = C::QR, NP = C::NP;
   constexpr int NCHUNK = D / 64;
-  constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DV = 256, TM_DK = 256 + D;
-  constexpr uint32_t IDESC_SQ = make_idesc_bf16(kBM, kBQ, 0, 0);  // St, dPt: N = q
-  constexpr uint32_t IDESC_KV = make_idesc_bf16(kBM, D, 0, 1);    // dV, dK: A K-major, B MN-major
-  constexpr uint32_t IDESC_DQ = make_idesc_bf16(kBQ, D, 1, 1);    // dQ: A, B MN-major
+  constexpr uint32_t IDESC_SQ = make_idesc_bf16(kBM, QR, 0, 0);  // St, dPt: N = q
+  constexpr uint32_t IDESC_KV = make_idesc_bf16(kBM, D, 0, 1);   // dV, dK: A K-major, B MN-major
+  constexpr uint32_t IDESC_DQ = make_idesc_bf16(QR, D, 1, 1);   // dQ: A, B MN-major
 
   const int nq = a.bt.nq;
   const BwdSmemLayout L = bwd_smem_layout(D, NQS, NOS, nq);
@@ -100,11 +123,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* bar_dp_full = bar_s_full + 1;
   uint64_t* bar_p_full = bar_s_full + 2;
   uint64_t* bar_ds_full = bar_s_full + 3;
-  uint64_t* bar_ds_empty = bar_s_full + 4;
-  uint64_t* bar_dq_full = bar_s_full + 5;
-  uint64_t* bar_dq_empty = bar_s_full + 6;
-  uint64_t* bar_dkv_full = bar_s_full + 7;
-  uint64_t* bar_teardown = bar_s_full + 8;
+  uint64_t* bar_dq_full = bar_s_full + 4;   // [2]
+  uint64_t* bar_dq_empty = bar_s_full + 6;  // [2]
+  uint64_t* bar_dkv_full = bar_s_full + 8;
+  uint64_t* bar_teardown = bar_s_full + 9;
   int* misc = reinterpret_cast<int*>(smem + L.misc_off);
   volatile int* abort_flag = misc;
   int* n_entries_s = misc + 1;
@@ -113,11 +135,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   int* entries = reinterpret_cast<int*>(smem + L.ent_off);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int BH = a.B * a.H;
-  const int bh = blockIdx.x % BH;
-  const int j = blockIdx.x / BH;  // kv tile; low j first (the most q tiles under causal masks)
+  const int bh = blockIdx.x % (a.B * a.H);
+  const int j = blockIdx.x / (a.B * a.H);  // kv tile; low j first (the most q tiles under causal masks)
   const int b = bh / a.H, h = bh % a.H;
-  const int Tq_pad = (a.Tq + kBQ - 1) / kBQ * kBQ;
+  const int Tq_pad = (a.Tq + 127) / 128 * 128;
 
   if (warp == kWarpProd && lane == 0) {
     mbar_init(bar_kv, 1);
@@ -133,9 +154,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar_dp_full, 1);
     mbar_init(bar_p_full, 256);
     mbar_init(bar_ds_full, 256);
-    mbar_init(bar_ds_empty, 1);
-    mbar_init(bar_dq_full, 1);
-    mbar_init(bar_dq_empty, 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_dq_full + s, 1);
+      mbar_init(bar_dq_empty + s, 128);
+    }
     mbar_init(bar_dkv_full, 1);
     mbar_init(bar_teardown, 1);
     misc[0] = 0;
@@ -167,14 +189,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   __syncthreads();
   if (warp == kWarpProd) {
+    // Step list: each listed 128-row q block becomes 128 / QR steps of QR rows (steps that
+    // start at or past Tq are dropped); entry = step index | class << 24 (1 partial, 2 full).
+    constexpr int SPB = 128 / QR;
     int base = 0;
     for (int i0 = 0; i0 < nq; i0 += 32) {
       const int i = i0 + lane;
       int c = (i < nq) ? cls[i] : 0;
       if (c == 3) c = 1;
-      const unsigned m = __ballot_sync(0xffffffffu, c != 0);
-      if (c) entries[base + __popc(m & ((1u << lane) - 1u))] = i | (c << 24);
-      base += __popc(m);
+      int ns = 0;
+      if (c)
+        for (int s = 0; s < SPB; ++s) ns += ((i * SPB + s) * QR < a.Tq);
+      int incl = ns;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      for (int s = 0; s < ns; ++s) entries[base + incl - ns + s] = (i * SPB + s) | (c << 24);
+      base += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) *n_entries_s = base;
   }
@@ -185,36 +218,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n_ent = *n_entries_s;
 
   if (warp >= kWarpProd) {
-    setmaxnreg_dec<kRegsCtl>();
+    setmaxnreg_dec<BwdRegs<D>::ctl>();
     if (warp == kWarpProd) {
       // ---------------------------------------------------------------- TMA producer
       if (lane == 0 && n_ent > 0) {
-        mbar_arrive_expect_tx(bar_kv, 2 * L.tile);
+        mbar_arrive_expect_tx(bar_kv, 2 * L.ktile);
         for (int c = 0; c < NCHUNK; ++c) {
-          tma_load_4d(sK + c * kChunk, &tm_k, bar_kv, c * 64, j * kBM, h, b);
-          tma_load_4d(sV + c * kChunk, &tm_v, bar_kv, c * 64, j * kBM, h, b);
+          tma_load_4d(sK + c * C::PANEL_K, &tm_k, bar_kv, c * 64, j * kBM, h, b);
+          tma_load_4d(sV + c * C::PANEL_K, &tm_v, bar_kv, c * 64, j * kBM, h, b);
         }
         const float* lse2 = a.lse2 + (int64_t)bh * Tq_pad;
         const float* dl = a.delta + (int64_t)bh * Tq_pad;
         bool ok = true;
         int issued_q = 0, issued_o = 0;
         for (int t = 0; t < n_ent && ok; ++t) {
-          const int i = entries[t] & 0xFFFFFF;
+          const int sub = entries[t] & 0xFFFFFF;
           const int qs = t % NQS, qu = t / NQS;
           if (!mbar_wait(bar_q_empty + qs, (qu & 1) ^ 1, abort_flag)) { ok = false; break; }
-          // lse2 and delta ride with Q: the Q slot is released only after dSt is built, which
-          // is the last read of both (the dO slot is released earlier, after the dV MMA).
-          mbar_arrive_expect_tx(bar_q_full + qs, L.tile + 2 * kBQ * 4);
+          // lse2 and delta ride with Q: the Q slot is released after dK(t), the last reader
+          // of Q; the compute warps have read lse2 and delta before dK(t) is issued.
+          mbar_arrive_expect_tx(bar_q_full + qs, L.qtile + 2 * QR * 4);
           for (int c = 0; c < NCHUNK; ++c)
-            tma_load_4d(sQ + qs * L.tile + c * kChunk, &tm_q, bar_q_full + qs, c * 64, i * kBQ, h, b);
-          bulk_load(sLse + qs * kBQ, lse2 + i * kBQ, kBQ * 4, bar_q_full + qs);
-          bulk_load(sDl + qs * kBQ, dl + i * kBQ, kBQ * 4, bar_q_full + qs);
+            tma_load_4d(sQ + qs * L.qtile + c * C::PANEL_Q, &tm_q, bar_q_full + qs, c * 64, sub * QR, h, b);
+          bulk_load(sLse + qs * QR, lse2 + sub * QR, QR * 4, bar_q_full + qs);
+          bulk_load(sDl + qs * QR, dl + sub * QR, QR * 4, bar_q_full + qs);
           ++issued_q;
           const int os = t % NOS, ou = t / NOS;
           if (!mbar_wait(bar_o_empty + os, (ou & 1) ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(bar_o_full + os, L.tile);
+          mbar_arrive_expect_tx(bar_o_full + os, L.qtile);
           for (int c = 0; c < NCHUNK; ++c)
-            tma_load_4d(sO + os * L.tile + c * kChunk, &tm_do, bar_o_full + os, c * 64, i * kBQ, h, b);
+            tma_load_4d(sO + os * L.qtile + c * C::PANEL_Q, &tm_do, bar_o_full + os, c * 64, sub * QR, h, b);
           ++issued_o;
         }
         if (!ok) {
@@ -235,109 +268,155 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (warp == kWarpMma) {
       // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0 && n_ent > 0) {
+      // The whole warp runs this loop with warp-uniform values (descriptors stay in uniform
+      // registers); elect.sync picks the lane that issues each tcgen05 instruction.
+      if (n_ent > 0) {
         // Descriptors are built once; per K step only the start-address field of the low
-        // word moves (see mma_ss_lh).  K-major: LBO 16 B; MN-major: LBO = one 64-column
-        // panel; SBO = 1024 B for both.  kofs/mofs are the per-step offsets in 16-byte units.
+        // word moves (see mma_ss_w).  K-major: LBO 16 B; MN-major: LBO = the operand's
+        // 64-column panel stride; SBO = 1024 B for both.  Offsets are in 16-byte units.
         const uint64_t d0 = make_smem_desc(smem_u32(sK), 16, 1024, SMEM_SWIZZLE_128B);
         const uint32_t hi = (uint32_t)(d0 >> 32);
         const uint32_t kmaj = (uint32_t)d0 - ((smem_u32(sK) >> 4) & 0x3FFFu);  // LBO bits only
-        const uint32_t mnmaj = (uint32_t)make_smem_desc(0, kChunk, 1024, SMEM_SWIZZLE_128B);
+        const uint32_t mn_k = (uint32_t)make_smem_desc(0, C::PANEL_K, 1024, SMEM_SWIZZLE_128B);
+        const uint32_t mn_q = (uint32_t)make_smem_desc(0, C::PANEL_Q, 1024, SMEM_SWIZZLE_128B);
+        const uint32_t mn_s = (uint32_t)make_smem_desc(0, C::PANEL_S, 1024, SMEM_SWIZZLE_128B);
         auto lo = [](uint32_t lbo_bits, const void* p) { return lbo_bits + ((smem_u32(p) >> 4) & 0x3FFFu); };
-        const uint32_t K_k = lo(kmaj, sK), K_mn = lo(mnmaj, sK), V_k = lo(kmaj, sV), S_k = lo(kmaj, sdS),
-                       S_mn = lo(mnmaj, sdS);
-        const uint32_t Q_k0 = lo(kmaj, sQ), Q_mn0 = lo(mnmaj, sQ), O_k0 = lo(kmaj, sO), O_mn0 = lo(mnmaj, sO);
-        const uint32_t tile16 = (uint32_t)L.tile >> 4;
-        auto kofs = [](int kk) { return (uint32_t)((kk >> 2) * (kChunk >> 4) + (kk & 3) * 2); };
+        const uint32_t K_k = lo(kmaj, sK), K_mn = lo(mn_k, sK), V_k = lo(kmaj, sV), S_k = lo(kmaj, sdS),
+                       S_mn = lo(mn_s, sdS);
+        const uint32_t Q_k0 = lo(kmaj, sQ), Q_mn0 = lo(mn_q, sQ), O_k0 = lo(kmaj, sO), O_mn0 = lo(mn_q, sO);
+        const uint32_t qtile16 = (uint32_t)L.qtile >> 4;
+        // K-major operand, K step kk of 16 elements along 64-element panels of `panel` bytes
+        auto kofs = [](int kk, int panel) { return (uint32_t)((kk >> 2) * (panel >> 4) + (kk & 3) * 2); };
+        // MN-major operand, K step kk of 16 rows (two 1024-byte swizzle atoms)
         auto mofs = [](int kk) { return (uint32_t)(kk * (2048 >> 4)); };
-        bool ok = mbar_wait(bar_kv, 0, abort_flag);
+        // Pt columns for K step kk (16 q): WG w = kk / (NP/16) holds q [w*NP, (w+1)*NP)
+        // packed two per column at TM_S + w*NP.
+        auto pcol = [](int kk) { return (uint32_t)((kk / (NP / 16)) * NP + (kk % (NP / 16)) * 8); };
+
+        auto issue_s = [&](int t) -> bool {  // St(t) = K Q^T
+          const int qs = t % NQS;
+          if (!mbar_wait_w(bar_q_full + qs, (t / NQS) & 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t Q_k = Q_k0 + qs * qtile16;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss_w(tmem_base + C::TM_S, K_k + kofs(kk, C::PANEL_K), hi, Q_k + kofs(kk, C::PANEL_Q), hi, IDESC_SQ,
+                      kk > 0);
+          tc_commit_w(bar_s_full);
+          return true;
+        };
+        auto issue_dp = [&](int t) -> bool {  // dPt(t) = V dO^T
+          const int os = t % NOS;
+          if (!mbar_wait_w(bar_o_full + os, (t / NOS) & 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t O_k = O_k0 + os * qtile16;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss_w(tmem_base + C::TM_DP, V_k + kofs(kk, C::PANEL_K), hi, O_k + kofs(kk, C::PANEL_Q), hi,
+                      IDESC_SQ, kk > 0);
+          tc_commit_w(bar_dp_full);
+          return true;
+        };
+
+        bool ok = mbar_wait_w(bar_kv, 0, abort_flag);
         tc_fence_after();
+        if (ok) ok = issue_s(0);
+        if (ok) ok = issue_dp(0);
         for (int t = 0; t < n_ent && ok; ++t) {
           const int qs = t % NQS, os = t % NOS;
           const uint32_t ph = t & 1;
-          const uint32_t Q_k = Q_k0 + qs * tile16, Q_mn = Q_mn0 + qs * tile16;
-          const uint32_t O_k = O_k0 + os * tile16, O_mn = O_mn0 + os * tile16;
           const uint32_t acc0 = t > 0 ? 1u : 0u;
-          // St = K Q^T
-          if (!(ok = mbar_wait(bar_q_full + qs, (t / NQS) & 1, abort_flag))) break;
+          // dV += Pt dO
+          if (!(ok = mbar_wait_w(bar_p_full, ph, abort_flag))) break;
           tc_fence_after();
+          const uint32_t O_mn = O_mn0 + os * qtile16;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_ss_lh(tmem_base + TM_S, K_k + kofs(kk), hi, Q_k + kofs(kk), hi, IDESC_SQ, kk > 0);
-          tc_commit(bar_s_full);
-          // dPt = V dO^T (its columns also hold dQ of the previous step until drained)
-          if (!(ok = mbar_wait(bar_o_full + os, (t / NOS) & 1, abort_flag))) break;
-          if (t > 0 && !(ok = mbar_wait(bar_dq_empty, ph ^ 1, abort_flag))) break;
+          for (int kk = 0; kk < QR / 16; ++kk)
+            mma_ts_w(tmem_base + C::TM_DV, tmem_base + C::TM_S + pcol(kk), O_mn + mofs(kk), hi, IDESC_KV,
+                      kk > 0 ? 1u : acc0);
+          tc_commit_w(bar_o_empty + os);  // dPt(t) and dV(t), the readers of dO(t), are issued
+          // St(t+1): Pt(t) in the S columns is consumed by dV(t) ahead of it in the pipe
+          if (t + 1 < n_ent && !(ok = issue_s(t + 1))) break;
+          // dQ(t) = dS K (M = q, N = d), then dK(t).  With buffers of its own, dQ(t) goes to
+          // buffer t & 1 once the drain has emptied it; otherwise into the dP columns, which
+          // the compute warps have finished reading when they arrive on ds_full.
+          if (!(ok = mbar_wait_w(bar_ds_full, ph, abort_flag))) break;
+          const int qb = C::DQ_OWN ? (t & 1) : 0;
+          if (C::DQ_OWN && t >= 2 && !(ok = mbar_wait_w(bar_dq_empty + qb, ((t >> 1) & 1) ^ 1, abort_flag))) break;
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_ss_lh(tmem_base + TM_DP, V_k + kofs(kk), hi, O_k + kofs(kk), hi, IDESC_SQ, kk > 0);
-          tc_commit(bar_dp_full);
-          // dV += Pt dO  (Pt of q columns 0-63 at St cols 0-31, 64-127 at cols 64-95)
-          if (!(ok = mbar_wait(bar_p_full, ph, abort_flag))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kBQ / 16; ++kk)
-            mma_ts_lh(tmem_base + TM_DV, tmem_base + TM_S + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), O_mn + mofs(kk),
-                      hi, IDESC_KV, kk > 0 ? 1u : acc0);
-          tc_commit(bar_o_empty + os);
-          // dK += dSt Q ; dQ_i = dS K
-          if (!(ok = mbar_wait(bar_ds_full, ph, abort_flag))) break;
-          tc_fence_after();
-          // dQ first: the drain (and, through it, the next dPt) waits on it; dK runs meanwhile.
 #pragma unroll
           for (int kk = 0; kk < kBM / 16; ++kk)
-            mma_ss_lh(tmem_base + TM_DP, S_mn + mofs(kk), hi, K_mn + mofs(kk), hi, IDESC_DQ, kk > 0);
-          tc_commit(bar_dq_full);
+            mma_ss_w(tmem_base + C::TM_DQ + D * qb, S_mn + mofs(kk), hi, K_mn + mofs(kk), hi, IDESC_DQ, kk > 0);
+          tc_commit_w(bar_dq_full + qb);
+          const uint32_t Q_mn = Q_mn0 + qs * qtile16;
 #pragma unroll
-          for (int kk = 0; kk < kBQ / 16; ++kk)
-            mma_ss_lh(tmem_base + TM_DK, S_k + kofs(kk), hi, Q_mn + mofs(kk), hi, IDESC_KV, kk > 0 ? 1u : acc0);
-          tc_commit(bar_q_empty + qs);
-          tc_commit(bar_ds_empty);
+          for (int kk = 0; kk < QR / 16; ++kk)
+            mma_ss_w(tmem_base + C::TM_DK, S_k + kofs(kk, C::PANEL_S), hi, Q_mn + mofs(kk), hi, IDESC_KV,
+                      kk > 0 ? 1u : acc0);
+          tc_commit_w(bar_q_empty + qs);
+          // dPt(t+1): the compute warps finished reading dPt(t) before arriving on ds_full;
+          // when dQ shares the dP columns, the drain must also have emptied them.
+          if (t + 1 < n_ent) {
+            if (!C::DQ_OWN && !(ok = mbar_wait_w(bar_dq_empty, t & 1, abort_flag))) break;
+            if (!(ok = issue_dp(t + 1))) break;
+          }
         }
-        if (ok) tc_commit(bar_dkv_full);
-        if (!ok) {
+        if (ok) tc_commit_w(bar_dkv_full);
+        if (!ok && lane == 0) {
           report_status(a.status, FA_ERR_TIMEOUT);
           *abort_flag = 1;
         }
-        tc_commit(bar_teardown);
+        tc_commit_w(bar_teardown);
         volatile int never = 0;
         mbar_wait(bar_teardown, 0, &never);
       }
       __syncwarp();
     }
   } else if (warp >= kWarpDq0) {
-    setmaxnreg_dec<kRegsDrain>();
-    // ------------------------------------------------------------------ dQ drain (thread = q row)
+    setmaxnreg_dec<BwdRegs<D>::drain>();
+    // ------------------------------------------------------------------ dQ drain (thread = lane)
+    // Per step: the D columns of dQ_t for this warp's 32 q rows, in 32-column chunks.  When
+    // the drain gates the next dPt (dQ in the dP columns), TMEM loads run two chunks ahead
+    // of the staging, so the buffer is released after the last load, not the last staging.
+    // A chunk is staged 128-byte swizzled in this warp's 4 KB buffer (rewritten only after
+    // the previous reduce has read it) and reduce-added by TMA.
+    constexpr int AHEAD = C::DQ_OWN ? 1 : 2;  // chunks held in registers
     const int wq = warp & 3;
-    const uint32_t t_dq = tmem_base + ((uint32_t)(wq * 32) << 16) + TM_DP;
     uint8_t* stage = sDq + wq * kDqStage;
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
-      const int i = entries[t] & 0xFFFFFF;
-      if (!(ok = mbar_wait(bar_dq_full, t & 1, abort_flag))) break;
+      const int sub = entries[t] & 0xFFFFFF;
+      const int qb = C::DQ_OWN ? (t & 1) : 0;
+      const uint32_t use = C::DQ_OWN ? (t >> 1) : t;  // completions of this buffer so far
+      if (!(ok = mbar_wait(bar_dq_full + qb, use & 1, abort_flag))) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_dq + c0, v);
-        tmem_ld_wait();
-        reg_pin(v);
-        if (c0 + 32 == D) {  // all of dQ_i is in registers: its TMEM columns may be reused
+      const uint32_t t_dq = tmem_base + ((uint32_t)(wq * 32) << 16) + C::TM_DQ + D * qb;
+      uint32_t v[AHEAD][32];
+#pragma unroll
+      for (int c = 0; c < AHEAD; ++c) tmem_ld32(t_dq + 32 * c, v[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        reg_pin(v[c % AHEAD]);
+        if (c == D / 32 - AHEAD) {  // every chunk is in registers or staged: release the buffer
           tc_fence_before();
-          mbar_arrive(bar_dq_empty);
+          mbar_arrive(bar_dq_empty + qb);
         }
-        if (lane == 0) bulk_wait_read_all();  // the previous reduce has read the stage
+        if (lane == 0) bulk_wait_read_all();
         __syncwarp();
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+              make_uint4(v[c % AHEAD][4 * u], v[c % AHEAD][4 * u + 1], v[c % AHEAD][4 * u + 2], v[c % AHEAD][4 * u + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_3d(&tm_dq, stage, c0, i * kBQ + wq * 32, bh);
+          tma_reduce_add_3d(&tm_dq, stage, 32 * c, sub * QR + wq * 32, bh);  // [BH, Tq, D]: x = d, y = q
           bulk_commit_group();
+        }
+        if (c + AHEAD < D / 32) {  // chunk c is staged: its registers take chunk c + AHEAD
+          tmem_ld32(t_dq + 32 * (c + AHEAD), v[c % AHEAD]);
+          tmem_ld_wait();
         }
       }
     }
@@ -347,13 +426,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       *abort_flag = 1;
     }
   } else {
-    setmaxnreg_inc<kRegsCompute>();
+    setmaxnreg_inc<BwdRegs<D>::compute>();
     // ------------------------------------------------------------------ compute (thread = kv row)
     const int wg = warp >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const int kv = j * kBM + r;
-    const int cbase = wg * 64;
+    const int cbase = wg * NP;  // first q column (within the step) of this warpgroup
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
@@ -373,23 +452,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];
-      const int i = e & 0xFFFFFF;
+      const int sub = e & 0xFFFFFF;
       const bool partial = ((e >> 24) & 3) == 1;
       const int qs = t % NQS;
       const uint32_t ph = t & 1;
-      const float* lse2 = sLse + qs * kBQ + cbase;
-      const float* dl = sDl + qs * kBQ + cbase;
-      const int q0 = i * kBQ + cbase;
+      const float* lse2 = sLse + qs * QR + cbase;
+      const float* dl = sDl + qs * QR + cbase;
+      const int q0 = sub * QR + cbase;  // local q of this thread's first column
 
       if (!(ok = mbar_wait(bar_s_full, ph, abort_flag))) break;
       tc_fence_after();
-      // p stays fp32 until dSt is formed; each 32-column half of Pt goes back to TMEM (bf16,
-      // into already-read S columns) as soon as it is computed, to keep registers low.
-      float p[64];
+      // p stays fp32 until dSt is formed; each 32-column group of Pt goes back to TMEM (bf16,
+      // into already-read S columns) as soon as it is computed.
+      float p[NP];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < NP / 32; ++hh) {
         uint32_t s[32];
-        tmem_ld32(t_lane + TM_S + cbase + 32 * hh, s);
+        tmem_ld32(t_lane + C::TM_S + cbase + 32 * hh, s);
         float l2[32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -398,7 +477,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tmem_ld_wait();
         reg_pin(s);
-        const int qg0 = q0 + 32 * hh + mc.q_off;  // global position of column 0 of this half
+        const int qg0 = q0 + 32 * hh + mc.q_off;  // global position of column 0 of this group
 #pragma unroll
         for (int c = 0; c < 32; ++c)
           p[32 * hh + c] = ex2_approx(score_log2<SK>(__uint_as_float(s[c]), qg0 + c, kvg, sc) - l2[c]);
@@ -420,20 +499,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) pk[c] = pack_bf16x2(p[32 * hh + 2 * c], p[32 * hh + 2 * c + 1]);
-        tmem_st16(t_lane + TM_S + (wg ? 64 : 0) + 16 * hh, pk);
+        tmem_st16(t_lane + C::TM_S + cbase + 16 * hh, pk);
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar_p_full);
 
+      // dPt(t) is issued after dK(t-1), so when it completes dQ(t-1) and dK(t-1) have read
+      // dSt(t-1) and the dSt buffer may be rewritten.
       if (!(ok = mbar_wait(bar_dp_full, ph, abort_flag))) break;
-      if (t > 0 && !(ok = mbar_wait(bar_ds_empty, ph ^ 1, abort_flag))) break;
       tc_fence_after();
-      uint8_t* ds_row = sdS + wg * kChunk + r * 128;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < NP / 32; ++hh) {
         uint32_t dp[32];
-        tmem_ld32(t_lane + TM_DP + cbase + 32 * hh, dp);
+        tmem_ld32(t_lane + C::TM_DP + cbase + 32 * hh, dp);
         float dl32[32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -460,9 +539,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           pk[c >> 1] = pack_bf16x2(d0, d1);
         }
+        const int qq = cbase + 32 * hh;  // first q column (within the step) of this group
+        uint8_t* ds_row = sdS + (qq >> 6) * C::PANEL_S + r * 128;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int unit = 4 * hh + u;  // 16-byte unit within the 128-byte row
+          const int unit = ((qq & 63) >> 3) + u;  // 16-byte unit within the 128-byte row
           *reinterpret_cast<uint4*>(ds_row + ((unit ^ (r & 7)) << 4)) =
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
@@ -493,7 +574,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int which = 0; which < 2; ++which) {
       const float mul = which ? a.scale : 1.f;
       __nv_bfloat16* dst = which ? dkr : dvr;
-      const uint32_t tcol = which ? TM_DK : TM_DV;
+      const uint32_t tcol = which ? C::TM_DK : C::TM_DV;
 #pragma unroll 1
       for (int c0 = wg * (D / 2); c0 < (wg + 1) * (D / 2); c0 += 32) {
         uint32_t v[32];
@@ -527,7 +608,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 bool pick_stages(int D, int nq, int* nqs, int* nos) {
-  const int cand[4][2] = {{2, 2}, {2, 1}, {1, 1}, {0, 0}};
+  const int cand[7][2] = {{4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}, {2, 1}, {0, 0}};
   for (int c = 0; cand[c][0]; ++c)
     if (bwd_smem_layout(D, cand[c][0], cand[c][1], nq).total <= 227 * 1024) {
       *nqs = cand[c][0];
@@ -544,20 +625,24 @@ int bwd_tc_max_stages(int D, int nq) {
   return pick_stages(D, nq, &a, &b) ? a : 0;
 }
 
+int bwd_tc_q_rows(int D) { return D == 128 ? BwdCfg<128>::QR : BwdCfg<64>::QR; }
+
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream) {
   int nqs = 0, nos = 0;
   if (!pick_stages(a.D, a.bt.nq, &nqs, &nos)) return cudaErrorInvalidValue;
-  if (a.num_stages > 0 && a.num_stages < nqs) nqs = a.num_stages;
+  if (a.num_stages >= 2 && a.num_stages < nqs) nqs = a.num_stages;
+  if (nos > nqs) nos = nqs;
   const int smem = bwd_smem_layout(a.D, nqs, nos, a.bt.nq).total;
   const dim3 grid((unsigned)(a.bt.nkv * a.B * a.H));
   const int sk = score_kind_of(a.score.flags);
-  auto go = [&](auto kern) -> cudaError_t {
+  auto go = [&](auto kern, auto regs) -> cudaError_t {
     // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.
+    using R = decltype(regs);
     cudaFuncAttributes fa_attr;
     cudaError_t e = cudaFuncGetAttributes(&fa_attr, kern);
     if (e != cudaSuccess) return e;
-    if (fa_attr.numRegs * kBwdThreads < 2 * 128 * kRegsCompute + 128 * kRegsDrain + 128 * kRegsCtl)
+    if (fa_attr.numRegs * kBwdThreads < 2 * 128 * R::compute + 128 * R::drain + 128 * R::ctl)
       return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -565,7 +650,7 @@ cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
     return cudaGetLastError();
   };
 #define FA_BWD_CASE(DD, SKK) \
-  if (a.D == DD && sk == SKK) return go(bwd_tc_kernel<DD, SKK>);
+  if (a.D == DD && sk == SKK) return go(bwd_tc_kernel<DD, SKK>, BwdRegs<DD>{});
   FA_BWD_CASE(128, SC_NONE)
   FA_BWD_CASE(128, SC_ALIBI)
   FA_BWD_CASE(128, SC_SOFTCAP)

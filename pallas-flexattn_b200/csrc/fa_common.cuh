@@ -148,7 +148,7 @@ struct AttnArgs {
   int Tq_pad;           // Tq rounded up to 128: row length of lse2 and delta
   float* lse2;          // [B*H, Tq_pad] lse * log2(e); +inf on padding and empty rows
   float* delta;         // [B*H, Tq_pad] rowsum(O * dO); 0 on padding
-  float* dq_accum;      // [B*H, Tq, D] fp32 dQ accumulator (unscaled)
+  float* dq_accum;      // [B*H, Tq, D] fp32 dQ accumulator (unscaled); room for B*H*Tq_pad*D
   float scale;
   FaMaskSpec mask;
   FaScoreSpec score;

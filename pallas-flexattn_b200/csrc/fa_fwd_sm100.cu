@@ -110,10 +110,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   int* entries = reinterpret_cast<int*>(smem + L.ent_off);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int BH = a.B * a.H;
   const int npairs = (a.bt.nq + 1) >> 1;
-  const int bh = blockIdx.x % BH;
-  const int pair = npairs - 1 - (int)(blockIdx.x / BH);  // heaviest (last) q rows first
+  const int bh = blockIdx.x % (a.B * a.H);
+  const int pair = npairs - 1 - (int)(blockIdx.x / (a.B * a.H));  // heaviest (last) q rows first
   const int b = bh / a.H, h = bh % a.H;
   const int hk = h / (a.H / a.Hkv);
 
