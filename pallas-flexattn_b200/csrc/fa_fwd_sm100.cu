@@ -231,19 +231,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // thread's serial chain of waits, MMAs and commits covers half the work.  Both walk
     // every kv entry and both commit to the K/V "empty" barriers (initialised with count
     // 2), so a slot is released only after both sub-tiles' MMAs that read it retired.
+    // The whole warp runs the loop with warp-uniform values (descriptors stay in uniform
+    // registers); elect.sync picks the lane that issues each tcgen05 instruction.
     const int i = warp - 9;
-    if (lane == 0 && n_ent > 0) {
+    if (n_ent > 0) {
       const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
       int last_t = -1;
       for (int t = 0; t < n_ent; ++t)
         if ((entries[t] >> (24 + 2 * i)) & 3) last_t = t;
-      bool ok = mbar_wait(bar_q, 0, abort_flag);
+      bool ok = mbar_wait_w(bar_q, 0, abort_flag);
       tc_fence_after();
       uint32_t p_phase = 0;
       int pv_count = 0;
 
       // Descriptors are built once; per K step only the start-address field of the low
-      // word moves (see mma_ss_lh).  K-major operands (Q, K) use LBO 16 B, the MN-major
+      // word moves (see mma_ss_w).  K-major operands (Q, K) use LBO 16 B, the MN-major
       // V operand uses LBO = one 64-column panel; both use SBO = 1024 B (8 swizzled rows).
       const uint64_t dq_base = make_smem_desc(sQa, 16, 1024, SMEM_SWIZZLE_128B);
       const uint32_t desc_hi = (uint32_t)(dq_base >> 32);
@@ -256,7 +258,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // S_i(t) = Q_i K_t^T (if this sub-tile visits entry t), then release K_t's slot.
       auto issue_s = [&](int t, bool part) -> bool {
         const int slot = (2 * t) % NS;
-        if (!mbar_wait(bar_kv_full + slot, ((2 * t) / NS) & 1, abort_flag)) return false;
+        if (!mbar_wait_w(bar_kv_full + slot, ((2 * t) / NS) & 1, abort_flag)) return false;
         if (part) {
           tc_fence_after();
           const uint32_t klo = k_lo0 + slot * tile16;
@@ -264,11 +266,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int kk = 0; kk < D / 16; ++kk) {
             constexpr uint32_t kChunk16 = CHUNK_BYTES >> 4;
             const uint32_t off = (kk >> 2) * kChunk16 + (kk & 3) * 2;
-            mma_ss_lh(s_dst, q_lo + off, desc_hi, klo + off, desc_hi, IDESC_S, kk > 0);
+            mma_ss_w(s_dst, q_lo + off, desc_hi, klo + off, desc_hi, IDESC_S, kk > 0);
           }
-          tc_commit(bar_s_full + i);
+          tc_commit_w(bar_s_full + i);
         }
-        tc_commit(bar_kv_empty + slot);
+        tc_commit_w(bar_kv_empty + slot);
         return true;
       };
       // O_i += P_i V_t (if visited), then release V_t's slot.  The slot's load is awaited
@@ -277,20 +279,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // released the current one (the empty barrier counts two arrivals per use).
       auto issue_pv = [&](int t, bool part) -> bool {
         const int slot = (2 * t + 1) % NS;
-        if (!mbar_wait(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
+        if (!mbar_wait_w(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
         if (part) {
-          if (!mbar_wait(bar_p_full + i, p_phase, abort_flag)) return false;
+          if (!mbar_wait_w(bar_p_full + i, p_phase, abort_flag)) return false;
           p_phase ^= 1;
           tc_fence_after();
           const uint32_t vlo = v_lo0 + slot * tile16;
           const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts_lh(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+            mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
           ++pv_count;
-          if (t == last_t) tc_commit(bar_o_full + i);
+          if (t == last_t) tc_commit_w(bar_o_full + i);
         }
-        tc_commit(bar_kv_empty + slot);
+        tc_commit_w(bar_kv_empty + slot);
         return true;
       };
 
@@ -299,12 +301,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ok = issue_pv(t, ((entries[t] >> (24 + 2 * i)) & 3) != 0);
         if (ok && t + 1 < n_ent) ok = issue_s(t + 1, ((entries[t + 1] >> (24 + 2 * i)) & 3) != 0);
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         report_status(a.status, FA_ERR_TIMEOUT);
         *abort_flag = 1;
       }
       // Teardown: wait (bounded) until every MMA this thread issued has retired.
-      tc_commit(bar_teardown + i);
+      tc_commit_w(bar_teardown + i);
       volatile int never = 0;
       mbar_wait(bar_teardown + i, 0, &never);
     }
