@@ -332,7 +332,8 @@ def main():
     traffic = None
     prof = REPO / "profiles" / "traffic.json"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get(f"{w.name}:{dominant}")
+        entry = json.loads(prof.read_text()).get(f"{w.name}:{dominant}")
+        traffic = entry["bytes"] if isinstance(entry, dict) else entry  # DRAM bytes per launch (ncu)
 
     e2e = None
     if not args.no_e2e:
@@ -375,7 +376,10 @@ def main():
                     "pct_of_2250": 100 * fwd_tf / 2250.0, "kernel": "tcgen05" if plan.tc else "simt"},
             "bwd": {"ms": ms_bwd, "tflops": bwd_tf, "pct_of_peak": 100 * bwd_tf / peak,
                     "pct_of_2250": 100 * bwd_tf / 2250.0},
-            "roofline": {"bound": "tensor", "kernel": dominant, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor",
+                         "kernel": ("bwd: one fa_bwd call = preprocess + bwd_tc + dq_convert launches"
+                                    if dominant == "bwd" else "fwd: fwd_tc (one launch)"),
+                         "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                          "frac": ach / peak, "peak_source": f"bf16_tflops ({peaks['source']})",
                          "traffic": traffic},
             "cpu_baseline": cpu,
