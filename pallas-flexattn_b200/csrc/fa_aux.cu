@@ -2,11 +2,14 @@
 //
 //   bwd_preprocess  delta = rowsum(O * dO) in fp32 (reference:
 //                   flash_attention_bwd_preprocess_kernel, src/pallas_flexattn/
-//                   flash_attn.py:168-173, which stores it in O's dtype) and zeroes
-//                   the fp32 dQ accumulator in the same pass.
+//                   flash_attn.py:168-173, which stores it in O's dtype) and
+//                   lse2 = lse * log2(e); the fp32 dQ accumulator is zeroed by a
+//                   memset on the same stream.
 //   dq_convert      dQ = scale * dq_accum, cast to the input dtype.
 //   lse_merge       combine two partial (O, logsumexp) results over disjoint keys.
-// One warp per row; each lane moves 16-byte vectors where alignment allows.
+// bf16 rows of 64 or 128 elements (16-byte aligned) take the vector kernels: a few
+// lanes per row, 16-byte loads, several rows per warp with every load issued before
+// the first use.  Other shapes take one warp per row.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -25,13 +28,6 @@ __device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// Zeroes D floats of the dQ accumulator per padded row, B*H*Tq_pad*D in all (the
-// [B*H, Tq, D] accumulator is the first B*H*Tq*D of them).
-__device__ __forceinline__ void zero_dq_row(const AttnArgs& a, int64_t prow, int lane) {
-  float4* z = reinterpret_cast<float4*>(a.dq_accum + prow * a.D);
-  for (int d4 = lane; d4 < a.D / 4; d4 += 32) z[d4] = make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
 // One warp per row of the padded [B*H, Tq_pad] grid.  Rows past Tq get delta = 0
 // and lse2 = +inf (so exp2(x - lse2) = 0 there); rows with lse = -inf (no key)
 // also get lse2 = +inf.
@@ -48,7 +44,6 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const Attn
       a.delta[prow] = 0.f;
       if (a.lse2) a.lse2[prow] = INFINITY;
     }
-    zero_dq_row(a, prow, lane);
     return;
   }
   const int64_t row = (int64_t)bh * a.Tq + t;
@@ -80,7 +75,6 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) preprocess_kernel(const Attn
       a.lse2[prow] = (l == -INFINITY) ? INFINITY : l * kLog2e;
     }
   }
-  zero_dq_row(a, prow, lane);
 }
 
 template <typename T>
@@ -121,10 +115,110 @@ __global__ void __launch_bounds__(kRowsPerCta * 32)
   if (lane == 0) lse_acc[row] = mx + logf(tot);
 }
 
+constexpr int kVecPasses = 4;  // rows per lane group in flight
+
+// Vector preprocess for bf16 rows of D = 64 or 128: L = D / 8 lanes per row (16 bytes
+// each), 32 / L rows per pass, kVecPasses passes per warp, one warp-row group per pass.
+template <int D>
+__global__ void __launch_bounds__(256) preprocess_bf16_vec_kernel(const AttnArgs a) {
+  constexpr int L = D / 8, RPP = 32 / L, RPW = RPP * kVecPasses;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / L, li = lane % L;
+  const int64_t prows = (int64_t)a.B * a.H * a.Tq_pad;
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * RPW;
+  uint4 ov[kVecPasses], gv[kVecPasses];
+#pragma unroll
+  for (int p = 0; p < kVecPasses; ++p) {
+    const int64_t prow = row0 + p * RPP + sub;
+    const int t = (int)(prow % a.Tq_pad);
+    const int bh = (int)(prow / a.Tq_pad), b = bh / a.H, h = bh % a.H;
+    ov[p] = gv[p] = make_uint4(0u, 0u, 0u, 0u);
+    if (prow < prows && t < a.Tq) {
+      ov[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
+                                              (int64_t)h * a.o.stride_h + (int64_t)t * a.o.stride_t + li * 8);
+      gv[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.dout.ptr) +
+                                              (int64_t)b * a.dout.stride_b + (int64_t)h * a.dout.stride_h +
+                                              (int64_t)t * a.dout.stride_t + li * 8);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < kVecPasses; ++p) {
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[p]);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[p]);
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 of = __bfloat1622float2(o2[u]), gf = __bfloat1622float2(g2[u]);
+      acc = fmaf(of.x, gf.x, fmaf(of.y, gf.y, acc));
+    }
+#pragma unroll
+    for (int off = L / 2; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    const int64_t prow = row0 + p * RPP + sub;
+    if (li == 0 && prow < prows) {
+      const int t = (int)(prow % a.Tq_pad);
+      const int64_t row = (prow / a.Tq_pad) * a.Tq + t;
+      a.delta[prow] = t < a.Tq ? acc : 0.f;
+      if (a.lse2) {
+        const float l = t < a.Tq ? a.lse_in[row] : -INFINITY;
+        a.lse2[prow] = (l == -INFINITY) ? INFINITY : l * kLog2e;
+      }
+    }
+  }
+}
+
+// Vector dQ conversion for bf16 output rows of D = 64 or 128: L = D / 4 lanes per row
+// (16 bytes of fp32 in, 8 bytes of bf16 out each).
+template <int D>
+__global__ void __launch_bounds__(256) dq_convert_bf16_vec_kernel(const AttnArgs a) {
+  constexpr int L = D / 4, RPP = 32 / L, RPW = RPP * kVecPasses;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / L, li = lane % L;
+  const int64_t rows = (int64_t)a.B * a.H * a.Tq;
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * RPW;
+  float4 v[kVecPasses];
+#pragma unroll
+  for (int p = 0; p < kVecPasses; ++p) {
+    const int64_t row = row0 + p * RPP + sub;
+    v[p] = row < rows ? *reinterpret_cast<const float4*>(a.dq_accum + row * D + li * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int p = 0; p < kVecPasses; ++p) {
+    const int64_t row = row0 + p * RPP + sub;
+    if (row >= rows) continue;
+    const int t = (int)(row % a.Tq);
+    const int bh = (int)(row / a.Tq), b = bh / a.H, h = bh % a.H;
+    __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(a.dq.ptr) + (int64_t)b * a.dq.stride_b +
+                        (int64_t)h * a.dq.stride_h + (int64_t)t * a.dq.stride_t + li * 4;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v[p].x * a.scale, v[p].y * a.scale);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(v[p].z * a.scale, v[p].w * a.scale);
+    uint2 w;
+    w.x = *reinterpret_cast<const uint32_t*>(&lo);
+    w.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dq) = w;
+  }
+}
+
+bool rows16(const FaTensor& t, int elem_bytes) {
+  return (reinterpret_cast<uintptr_t>(t.ptr) % 16 == 0) && ((t.stride_t * elem_bytes) % 16 == 0) &&
+         ((t.stride_h * elem_bytes) % 16 == 0) && ((t.stride_b * elem_bytes) % 16 == 0);
+}
+
 }  // namespace
 
 cudaError_t launch_bwd_preprocess(const AttnArgs& a, int dtype, cudaStream_t stream) {
   const int64_t rows = (int64_t)a.B * a.H * a.Tq_pad;
+  // The dQ accumulator: B*H*Tq_pad*D floats (all of it in the padded layout of fa_bwd,
+  // exactly [B*H, Tq, D] in the public preprocess entry point, where Tq_pad = Tq).
+  cudaError_t e = cudaMemsetAsync(a.dq_accum, 0, (size_t)rows * a.D * sizeof(float), stream);
+  if (e != cudaSuccess) return e;
+  const bool vec = dtype == FA_DTYPE_BF16 && (a.D == 64 || a.D == 128) && rows16(a.o, 2) && rows16(a.dout, 2);
+  if (vec) {
+    const int64_t per_cta = 8LL * kVecPasses * (32 / (a.D / 8));
+    const unsigned grid = (unsigned)((rows + per_cta - 1) / per_cta);
+    if (a.D == 128) preprocess_bf16_vec_kernel<128><<<grid, 256, 0, stream>>>(a);
+    else preprocess_bf16_vec_kernel<64><<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
   if (dtype == FA_DTYPE_F32) preprocess_kernel<float><<<grid, kRowsPerCta * 32, 0, stream>>>(a);
   else preprocess_kernel<__nv_bfloat16><<<grid, kRowsPerCta * 32, 0, stream>>>(a);
@@ -133,6 +227,13 @@ cudaError_t launch_bwd_preprocess(const AttnArgs& a, int dtype, cudaStream_t str
 
 cudaError_t launch_dq_convert(const AttnArgs& a, int dtype, cudaStream_t stream) {
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
+  if (dtype == FA_DTYPE_BF16 && (a.D == 64 || a.D == 128) && rows16(a.dq, 2)) {
+    const int64_t per_cta = 8LL * kVecPasses * (32 / (a.D / 4));
+    const unsigned grid = (unsigned)((rows + per_cta - 1) / per_cta);
+    if (a.D == 128) dq_convert_bf16_vec_kernel<128><<<grid, 256, 0, stream>>>(a);
+    else dq_convert_bf16_vec_kernel<64><<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
   if (dtype == FA_DTYPE_F32) dq_convert_kernel<float><<<grid, kRowsPerCta * 32, 0, stream>>>(a);
   else dq_convert_kernel<__nv_bfloat16><<<grid, kRowsPerCta * 32, 0, stream>>>(a);

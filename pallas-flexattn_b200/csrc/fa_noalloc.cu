@@ -11,10 +11,11 @@
 // lazy module loading (the CUDA 12 default), at context creation under eager loading.
 // Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
 //
-// Per call, fa_bwd's preprocess kernel writes delta and lse2 and zeroes the fp32 dQ
-// accumulator (the only part that must start at zero) before the fused kernel reads it,
-// so no state carries from one call to the next.  Calls that overlap on one device
-// (several streams or host threads) share the array and race.
+// Per call, fa_bwd's preprocess step zeroes the fp32 dQ accumulator (a memset on the
+// caller's stream; the only part that must start at zero) and writes delta and lse2
+// before the fused kernel reads them, so no state carries from one call to the next.
+// Calls that overlap on one device (several streams or host threads) share the array
+// and race.
 #include <cuda_runtime.h>
 
 #include <atomic>
