@@ -68,7 +68,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv)
   L.q_off = 0;
   L.kv_off = 2 * L.tile_bytes;
   L.bar_off = L.kv_off + ns * L.tile_bytes;
-  L.misc_off = L.bar_off + (2 * ns + 12) * 8;
+  L.misc_off = L.bar_off + (2 * ns + 14) * 8;
   L.cls_off = L.misc_off + 16;
   L.ent_off = L.cls_off + 4 * nkv;
   L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
@@ -98,8 +98,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* bar_kv_full = bars + 1;
   uint64_t* bar_kv_empty = bars + 1 + NS;
   uint64_t* bar_s_full = bars + 1 + 2 * NS;   // [2]
-  uint64_t* bar_p_full = bar_s_full + 2;       // [2]
-  uint64_t* bar_o_full = bar_p_full + 2;       // [2]
+  uint64_t* bar_p_full = bar_s_full + 2;       // [2][2]: sub-tile i, kv half h (P columns 64h..64h+63)
+  uint64_t* bar_o_full = bar_p_full + 4;       // [2]
   uint64_t* bar_teardown = bar_o_full + 2;     // [2]
   uint64_t* bar_turn = bar_teardown + 2;       // [2] softmax ping-pong
   int* misc = reinterpret_cast<int*>(smem + L.misc_off);
@@ -125,7 +125,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + i, 1);
-      mbar_init(bar_p_full + i, 128);
+      mbar_init(bar_p_full + 2 * i, 128);
+      mbar_init(bar_p_full + 2 * i + 1, 128);
       mbar_init(bar_o_full + i, 1);
     }
     mbar_init(bar_teardown, 1);
@@ -281,14 +282,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int slot = (2 * t + 1) % NS;
         if (!mbar_wait_w(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
         if (part) {
-          if (!mbar_wait_w(bar_p_full + i, p_phase, abort_flag)) return false;
-          p_phase ^= 1;
-          tc_fence_after();
+          // P arrives in two halves of 64 kv columns; the first half's MMAs start while the
+          // softmax warps still compute the second.
           const uint32_t vlo = v_lo0 + slot * tile16;
           const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+          for (int hh = 0; hh < 2; ++hh) {
+            if (!mbar_wait_w(bar_p_full + 2 * i + hh, p_phase, abort_flag)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 4 * hh; kk < 4 * hh + 4; ++kk)
+              mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+          }
+          p_phase ^= 1;
           ++pv_count;
           if (t == last_t) tc_commit_w(bar_o_full + i);
         }
@@ -337,6 +343,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
 
+    // Turn-taking is compiled only where the host may enable it (no score_mod).
+    constexpr bool PP = SK == SC_NONE;
     float row_max = -INFINITY, row_sum = 0.f;
     uint32_t s_phase = 0;
     int processed = 0;
@@ -344,17 +352,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int t = 0; t < n_ent; ++t) {
       const int e = entries[t];
       const int code = (e >> (24 + 2 * i)) & 3;
-      // Ping-pong (when enabled): the two softmax warpgroups take strict turns (0, 1, 0, 1, ...),
-      // one turn per kv entry each, visited or not, so one warpgroup's exponentials run while
-      // the tensor cores work on the other sub-tile's PV and next S.  Turn k of warpgroup 0
-      // needs warpgroup 1's (k-1)-th hand-over; turn k of warpgroup 1 needs warpgroup 0's k-th.
-      if (pingpong) {
-        if (!mbar_wait(bar_turn + i, i == 0 ? ((t & 1) ^ 1) : (t & 1), abort_flag)) { ok = false; break; }
-        if (!code) {
+      // Ping-pong (when enabled): the two softmax warpgroups take strict turns (0, 1, 0, 1, ...)
+      // for their exponential loops, one turn per kv entry each, visited or not, so one
+      // warpgroup's exponentials run while the tensor cores work on the other sub-tile's PV and
+      // next S, and the row max (FMA pipe) overlaps the other warpgroup's exponentials (MUFU).
+      // Turn k of warpgroup 0 needs warpgroup 1's (k-1)-th hand-over; turn k of warpgroup 1
+      // needs warpgroup 0's k-th.
+      const uint32_t turn_parity = i == 0 ? ((t & 1) ^ 1) : (t & 1);
+      if (!code) {
+        if (PP && pingpong) {
+          if (!mbar_wait(bar_turn + i, turn_parity, abort_flag)) { ok = false; break; }
           mbar_arrive(bar_turn + (1 - i));
-          continue;
         }
-      } else if (!code) {
         continue;
       }
       const int kvg0 = (e & 0xFFFFFF) * kBN + mc.kv_off;  // global position of the tile's first key
@@ -396,14 +405,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (!mask_ok(mc, qg, kvg0 + c, dq_val)) x[c] = -INFINITY;
         }
       }
+      // Row max with three-input max: 8 accumulators over columns 0-119, then 120-127.
+      static_assert(kBN == 128, "the max tree below covers 128 columns");
       float m8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = x[k];
+      for (int k = 0; k < 8; ++k) m8[k] = fmax3f(x[k], x[8 + k], x[16 + k]);
 #pragma unroll
-      for (int c = 8; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
-      float mloc = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                         fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int c = 24; c < 120; c += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], x[c + 8 + k]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], x[120 + k]);
+      float mloc = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       if constexpr (SK == SC_NONE) mloc *= sc.k_log2;
+      if (PP && pingpong && !mbar_wait(bar_turn + i, turn_parity, abort_flag)) { ok = false; break; }
       float alpha = 1.f;
       const bool rescale = mloc > row_max + kRescaleThreshold;
       if (rescale) {
@@ -413,6 +428,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float m_use = (row_max == -INFINITY) ? 0.f : row_max;
       const float2 kk2 = make_float2(SK == SC_NONE ? sc.k_log2 : 1.f, SK == SC_NONE ? sc.k_log2 : 1.f);
       const float2 nm2 = make_float2(-m_use, -m_use);
+      // Rescale O before any of this entry's P is published (the PV MMAs that read the
+      // first half may start before the second is computed); PV(t-1) has retired, since S(t)
+      // was committed after it.
+      if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t ov[32];
+          tmem_ld32(tO + c0, ov);
+          tmem_ld_wait();
+          reg_pin(ov);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+          tmem_st32(tO + c0, ov);
+        }
+      }
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
       // Full tiles hold no -inf, so some exponentials may take the polynomial path.
@@ -434,27 +464,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #endif
         }
         tmem_st16(tS + (c0 >> 1), pk);
+        if (c0 % 64 == 32) {  // a 64-column half of P is written: publish it to the PV MMAs
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(bar_p_full + 2 * i + (c0 >> 6));
+        }
       }
+      if (PP && pingpong) mbar_arrive(bar_turn + (1 - i));  // exponentials issued: the other warpgroup's turn
       const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
       const float2 s4 = __fadd2_rn(s01, s23);
       const float sum = s4.x + s4.y;
       row_sum = row_sum * alpha + sum;
-      if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t ov[32];
-          tmem_ld32(tO + c0, ov);
-          tmem_ld_wait();
-          reg_pin(ov);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-          tmem_st32(tO + c0, ov);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar_p_full + i);
-      if (pingpong) mbar_arrive(bar_turn + (1 - i));
       ++processed;
     }
     if (!ok) {

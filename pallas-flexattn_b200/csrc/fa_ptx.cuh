@@ -312,6 +312,12 @@ __device__ __forceinline__ void red_add_v4_f32(float* p, uint4 v) {
                "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
                : "memory");
 }
+// Three-input maximum (max.f32 with three sources, sm_100).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ float lg2_approx(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
