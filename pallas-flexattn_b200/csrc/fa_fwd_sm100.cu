@@ -48,6 +48,10 @@ constexpr int kRegsSoftmax = 216, kRegsCtl = 72;
 #ifndef FA_FWD_EXP_EMU
 #define FA_FWD_EXP_EMU 0
 #endif
+// P is published to the PV MMAs in FA_FWD_P_PARTS parts of 128 / FA_FWD_P_PARTS kv columns.
+#ifndef FA_FWD_P_PARTS
+#define FA_FWD_P_PARTS 2
+#endif
 // Softmax ping-pong: -1 chooses per launch, 0 forces it off, 1 forces it on.
 #ifndef FA_FWD_PINGPONG
 #define FA_FWD_PINGPONG -1
@@ -68,7 +72,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv)
   L.q_off = 0;
   L.kv_off = 2 * L.tile_bytes;
   L.bar_off = L.kv_off + ns * L.tile_bytes;
-  L.misc_off = L.bar_off + (2 * ns + 14) * 8;
+  L.misc_off = L.bar_off + (2 * ns + 10 + 2 * FA_FWD_P_PARTS) * 8;
   L.cls_off = L.misc_off + 16;
   L.ent_off = L.cls_off + 4 * nkv;
   L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
@@ -98,8 +102,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* bar_kv_full = bars + 1;
   uint64_t* bar_kv_empty = bars + 1 + NS;
   uint64_t* bar_s_full = bars + 1 + 2 * NS;   // [2]
-  uint64_t* bar_p_full = bar_s_full + 2;       // [2][2]: sub-tile i, kv half h (P columns 64h..64h+63)
-  uint64_t* bar_o_full = bar_p_full + 4;       // [2]
+  uint64_t* bar_p_full = bar_s_full + 2;       // [2][FA_FWD_P_PARTS]: sub-tile i, part h of P
+  uint64_t* bar_o_full = bar_p_full + 2 * FA_FWD_P_PARTS;  // [2]
   uint64_t* bar_teardown = bar_o_full + 2;     // [2]
   uint64_t* bar_turn = bar_teardown + 2;       // [2] softmax ping-pong
   int* misc = reinterpret_cast<int*>(smem + L.misc_off);
@@ -125,8 +129,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + i, 1);
-      mbar_init(bar_p_full + 2 * i, 128);
-      mbar_init(bar_p_full + 2 * i + 1, 128);
+      for (int h = 0; h < FA_FWD_P_PARTS; ++h) mbar_init(bar_p_full + FA_FWD_P_PARTS * i + h, 128);
       mbar_init(bar_o_full + i, 1);
     }
     mbar_init(bar_teardown, 1);
@@ -282,16 +285,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int slot = (2 * t + 1) % NS;
         if (!mbar_wait_w(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
         if (part) {
-          // P arrives in two halves of 64 kv columns; the first half's MMAs start while the
-          // softmax warps still compute the second.
+          // P arrives in FA_FWD_P_PARTS parts of kv columns; a part's MMAs start while the
+          // softmax warps still compute the next.
           const uint32_t vlo = v_lo0 + slot * tile16;
           const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
+          constexpr int KPP = kBN / 16 / FA_FWD_P_PARTS;  // K steps per part
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            if (!mbar_wait_w(bar_p_full + 2 * i + hh, p_phase, abort_flag)) return false;
+          for (int hh = 0; hh < FA_FWD_P_PARTS; ++hh) {
+            if (!mbar_wait_w(bar_p_full + FA_FWD_P_PARTS * i + hh, p_phase, abort_flag)) return false;
             tc_fence_after();
 #pragma unroll
-            for (int kk = 4 * hh; kk < 4 * hh + 4; ++kk)
+            for (int kk = KPP * hh; kk < KPP * hh + KPP; ++kk)
               mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
           }
           p_phase ^= 1;
@@ -464,10 +468,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #endif
         }
         tmem_st16(tS + (c0 >> 1), pk);
-        if (c0 % 64 == 32) {  // a 64-column half of P is written: publish it to the PV MMAs
+        constexpr int PW = kBN / FA_FWD_P_PARTS;  // kv columns per published part
+        if ((c0 + 32) % PW == 0) {  // a part of P is written: publish it to the PV MMAs
           tmem_st_wait();
           tc_fence_before();
-          mbar_arrive(bar_p_full + 2 * i + (c0 >> 6));
+          mbar_arrive(bar_p_full + FA_FWD_P_PARTS * i + c0 / PW);
         }
       }
       if (PP && pingpong) mbar_arrive(bar_turn + (1 - i));  // exponentials issued: the other warpgroup's turn
