@@ -181,6 +181,47 @@ def max_over_ranks(dist, x: float, device) -> float:
     return float(t.item())
 
 
+def parity_check(w, q, k, v, do) -> dict:
+    """One (b, h) slice of the bench's own inputs through the public API (forward and
+    autograd backward) against the materialised fp32 torch reference, with the parity bar:
+    rel-L2 <= 5e-3 and |err| <= 2e-2 + 2^-8 |ref| per element."""
+    import pallas_flexattn as pf
+    from pallas_flexattn.flash_attn import mha_reference
+
+    sl = [t.detach()[:1, :1].contiguous() for t in (q, k, v, do)]
+    qq, kk, vv = (t.clone().requires_grad_(True) for t in sl[:3])
+    o = pf.flash_attention(qq, kk, vv, w.mask_mod, score_mod=w.score_mod)
+    got = (o, *torch.autograd.grad(o, (qq, kk, vv), sl[3]))
+    qf, kf, vf = (t.float().requires_grad_(True) for t in sl[:3])
+    of = mha_reference(qf, kf, vf, w.mask_mod, score_mod=w.score_mod)
+    ref = (of, *torch.autograd.grad(of, (qf, kf, vf), sl[3].float()))
+    res, ok = {}, True
+    for name, g, r in zip(("o", "dq", "dk", "dv"), got, ref):
+        g, r = g.detach().float(), torch.nan_to_num(r.detach().float())
+        diff = (g - r).abs()
+        excess = float((diff - (2e-2 + 2.0 ** -8 * r.abs())).max())
+        rel = float((g - r).norm() / r.norm().clamp_min(1e-30))
+        res[name] = {"max_abs": round(float(diff.max()), 6), "rel_l2": round(rel, 7)}
+        ok = ok and excess <= 0 and rel <= 5e-3
+    res["slice"] = "b=0, h=0 of the timed inputs"
+    res["pass"] = ok
+    return res
+
+
+def block_mask_ms(w, device, reps: int = 5) -> float:
+    """Wall time of create_block_mask for the workload's mask (GPU tables), after warm-up."""
+    from pallas_flexattn.block_mask import create_block_mask
+
+    for _ in range(2):
+        create_block_mask(w.mask_mod, w.B, w.H, w.S, w.S, 128, device=device)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        create_block_mask(w.mask_mod, w.B, w.H, w.S, w.S, 128, device=device)
+    torch.cuda.synchronize(device)
+    return (time.perf_counter() - t0) / reps * 1e3
+
+
 def cpu_baseline(w, n_pairs: int, budget_s: float = 12.0) -> dict:
     """Time the reference's tiled CPU path (torch restatement) on one (b, h) slice."""
     from oracle import cpu_reference as ref
@@ -358,6 +399,8 @@ def main():
                "h2d_bytes_per_step": 4 * q.numel() * q.element_size(),
                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(), "ms_per_step": ms_e2e}
 
+    parity = parity_check(w, q, k, v, do)
+    bm_ms = block_mask_ms(w, device)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, n_pairs)
@@ -386,6 +429,8 @@ def main():
             "e2e": e2e,
             "clocks": clk.summary(),
             "gpu_launches": args.steps * (fwd_launches + bwd_launches),
+            "parity": parity,
+            "block_mask_ms": bm_ms,
             "unmasked_pairs_per_bh": n_pairs,
         }
         print(json.dumps(line), flush=True)

@@ -67,7 +67,11 @@ enum {
  * positions q + q_offset and kv + kv_offset, so a caller can run one block of a
  * longer sequence (the context-parallel ring does); document ids and the tile
  * table are indexed by global position. */
-enum { FA_MASK_CAUSAL = 1, FA_MASK_WINDOW = 2, FA_MASK_DOCUMENT = 4, FA_MASK_TILE_TABLE = 8 };
+enum { FA_MASK_CAUSAL = 1, FA_MASK_WINDOW = 2, FA_MASK_DOCUMENT = 4, FA_MASK_TILE_TABLE = 8,
+       /* with FA_MASK_DOCUMENT: the ids are non-decreasing along the sequence (contiguous
+          documents), so the tcgen05 kernels reduce "same document" to one position interval
+          per row instead of testing it per element */
+       FA_MASK_DOC_SORTED = 16 };
 
 typedef struct {
   int32_t flags;

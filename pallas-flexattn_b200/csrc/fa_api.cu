@@ -112,8 +112,10 @@ int check_common(int dtype, int B, int H, int Hkv, int Tq, int Tkv, int D, const
     return fail(FA_ERR_INVALID, "document mask without document ids");
   if ((m.flags & FA_MASK_TILE_TABLE) && (!m.tile_table || m.table_block <= 0 || m.table_cols <= 0))
     return fail(FA_ERR_INVALID, "tile-table mask without a table");
-  if (m.flags & ~(FA_MASK_CAUSAL | FA_MASK_WINDOW | FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE))
+  if (m.flags & ~(FA_MASK_CAUSAL | FA_MASK_WINDOW | FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE | FA_MASK_DOC_SORTED))
     return fail(FA_ERR_INVALID, "unknown mask flags 0x%x", m.flags);
+  if ((m.flags & FA_MASK_DOC_SORTED) && !(m.flags & FA_MASK_DOCUMENT))
+    return fail(FA_ERR_INVALID, "FA_MASK_DOC_SORTED needs FA_MASK_DOCUMENT");
   if (s.flags & ~(FA_SCORE_ALIBI | FA_SCORE_SOFTCAP | FA_SCORE_REL_BIAS))
     return fail(FA_ERR_INVALID, "unknown score flags 0x%x", s.flags);
   if ((s.flags & FA_SCORE_ALIBI) && !s.alibi_slopes) return fail(FA_ERR_INVALID, "ALiBi without slopes");

@@ -448,7 +448,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (mc.left >= 0) q_hi = min(q_hi, kvg + mc.left);
       if (mc.right >= 0) q_lo = max(q_lo, kvg - mc.right);
     }
-    const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
+    // Contiguous documents: the kv row's document is one q interval too.
+    const bool doc_iv = (mc.flags & FA_MASK_DOCUMENT) && (mc.flags & FA_MASK_DOC_SORTED);
+    if (doc_iv && kv < a.Tkv) {
+      int f, l;
+      doc_range(mc.doc_q, mc.q_off, mc.q_off + a.Tq, __ldg(mc.doc_kv + kvg), &f, &l);
+      q_lo = max(q_lo, f);
+      q_hi = min(q_hi, l);
+    }
+    const bool per_elem_mask = (mc.flags & FA_MASK_TILE_TABLE) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];

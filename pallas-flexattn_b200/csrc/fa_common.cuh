@@ -132,6 +132,26 @@ __device__ __forceinline__ bool mask_ok(const MaskCtx& m, int q, int kv, int dq)
   return ok;
 }
 
+// For non-decreasing document ids: the positions [*first, *last] within [lo, hi) whose id
+// equals d (an empty range gives *first > *last).  Two binary searches, log2(hi - lo)
+// steps each.
+__device__ inline void doc_range(const int32_t* doc, int lo, int hi, int d, int* first, int* last) {
+  int a = lo, b = hi;  // first position with id >= d
+  while (a < b) {
+    const int m = (a + b) >> 1;
+    if (__ldg(doc + m) < d) a = m + 1;
+    else b = m;
+  }
+  int c = a, e = hi;  // first position with id > d
+  while (c < e) {
+    const int m = (c + e) >> 1;
+    if (__ldg(doc + m) <= d) c = m + 1;
+    else e = m;
+  }
+  *first = a;
+  *last = c - 1;
+}
+
 // Row offset (in rows of nq / nkv entries) of the block tables for (b, h).
 __device__ __forceinline__ int64_t table_head(const FaBlockTables& t, int b, int h) {
   const int tb = t.num_b > 1 ? b : 0;

@@ -345,7 +345,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (mc.left >= 0) row_lo = max(row_lo, qg - mc.left);
       if (mc.right >= 0) row_hi = min(row_hi, qg + mc.right);
     }
-    const bool per_elem_mask = (mc.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE)) != 0;
+    // Contiguous documents: the row's document is one kv interval too.
+    const bool doc_iv = (mc.flags & FA_MASK_DOCUMENT) && (mc.flags & FA_MASK_DOC_SORTED);
+    if (doc_iv) {
+      int f, l;
+      doc_range(mc.doc_kv, mc.kv_off, mc.Tkv, dq_val, &f, &l);
+      row_lo = max(row_lo, f);
+      row_hi = min(row_hi, l);
+    }
+    const bool per_elem_mask = (mc.flags & FA_MASK_TILE_TABLE) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
 
     // Turn-taking is compiled only where the host may enable it (no score_mod).
     constexpr bool PP = SK == SC_NONE;
@@ -553,7 +561,9 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   // score_mod, no per-element mask predicate); a heavier softmax runs better with both
   // warpgroups in flight at once.
 #if FA_FWD_PINGPONG < 0
-  const int pingpong = a.D == 128 && sk == SC_NONE && !(a.mask.flags & (FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE));
+  const bool per_elem = (a.mask.flags & FA_MASK_TILE_TABLE) ||
+                        ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
+  const int pingpong = a.D == 128 && sk == SC_NONE && !per_elem;
 #else
   const int pingpong = FA_FWD_PINGPONG;
 #endif

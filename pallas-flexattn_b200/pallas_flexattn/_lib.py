@@ -14,7 +14,7 @@ from pathlib import Path
 FA_OK, FA_ERR_INVALID, FA_ERR_UNSUPPORTED, FA_ERR_CUDA, FA_ERR_TIMEOUT = 0, 1, 2, 3, 4
 FA_DTYPE_F32, FA_DTYPE_BF16 = 0, 1
 FA_KERNEL_AUTO, FA_KERNEL_TC, FA_KERNEL_SIMT = 0, 1, 2
-FA_MASK_CAUSAL, FA_MASK_WINDOW, FA_MASK_DOCUMENT, FA_MASK_TILE_TABLE = 1, 2, 4, 8
+FA_MASK_CAUSAL, FA_MASK_WINDOW, FA_MASK_DOCUMENT, FA_MASK_TILE_TABLE, FA_MASK_DOC_SORTED = 1, 2, 4, 8, 16
 FA_SCORE_ALIBI, FA_SCORE_SOFTCAP, FA_SCORE_REL_BIAS = 1, 2, 4
 FA_BLOCK_MASK_EXACT, FA_BLOCK_MASK_REF9 = 0, 1
 FA_NOALLOC_SCRATCH_BYTES = 64 << 20  # static scratch of fa_bwd_noalloc

@@ -34,6 +34,7 @@ class MaskSpec:
     window_left: int = -1
     window_right: int = -1
     doc_ids: Optional[torch.Tensor] = None     # [T] or [B, T] int32
+    doc_sorted: bool = False                   # ids non-decreasing along T (contiguous documents)
     tile_table: Optional[torch.Tensor] = None  # [rows, cols] uint8, nonzero = keep
     table_block: int = 0
     _dev: dict = field(default_factory=dict, repr=False, compare=False)
@@ -80,6 +81,8 @@ class MaskSpec:
             m.doc_q = doc.data_ptr()
             m.doc_kv = doc.data_ptr()
             m.doc_stride_b = T if (doc.dim() == 2 and doc.shape[0] > 1) else 0
+            if self.doc_sorted:
+                m.flags |= L.FA_MASK_DOC_SORTED
         if self.flags & L.FA_MASK_TILE_TABLE:
             t = dev["table"]
             m.tile_table = t.data_ptr()
@@ -146,15 +149,20 @@ def document_mask(seq_lengths, block_size: int = 128) -> MaskMod:
     signature compatibility and unused.
     """
     del block_size
-    lens = torch.as_tensor(np.asarray(seq_lengths), dtype=torch.int64)
-    if lens.dim() == 1:
-        doc = torch.repeat_interleave(torch.arange(lens.numel(), dtype=torch.int32), lens)
-    else:
-        rows = [torch.repeat_interleave(torch.arange(r.numel(), dtype=torch.int32), r) for r in lens]
-        if len({r.numel() for r in rows}) != 1:
-            raise ValueError("every batch row of seq_lengths must cover the same total length")
-        doc = torch.stack(rows)
-    return document_ids_mask(doc)
+
+    def ids(lens) -> torch.Tensor:
+        lens = torch.as_tensor(np.asarray(lens), dtype=torch.int64).reshape(-1)
+        return torch.repeat_interleave(torch.arange(lens.numel(), dtype=torch.int32), lens)
+
+    per_row = (isinstance(seq_lengths, (list, tuple)) and len(seq_lengths) > 0
+               and np.ndim(seq_lengths[0]) == 1) or (np.ndim(seq_lengths) == 2 if not isinstance(
+                   seq_lengths, (list, tuple)) else False)
+    if not per_row:
+        return document_ids_mask(ids(seq_lengths))
+    rows = [ids(r) for r in seq_lengths]  # batch rows may hold different numbers of documents
+    if len({r.numel() for r in rows}) != 1:
+        raise ValueError("every batch row of seq_lengths must cover the same total length")
+    return document_ids_mask(torch.stack(rows))
 
 
 def document_ids_mask(doc_ids) -> MaskMod:
@@ -170,7 +178,9 @@ def document_ids_mask(doc_ids) -> MaskMod:
             return d[q_idx.long()] == d[kv_idx.long()]
         return doc_np[np.asarray(q_idx)] == doc_np[np.asarray(kv_idx)]
 
-    return _with_spec(mask, MaskSpec(flags=L.FA_MASK_DOCUMENT, doc_ids=doc))
+    # Contiguous documents (non-decreasing ids) let the kernels use one interval per row.
+    doc_sorted = bool((doc[..., 1:] >= doc[..., :-1]).all()) if doc.shape[-1] > 1 else True
+    return _with_spec(mask, MaskSpec(flags=L.FA_MASK_DOCUMENT, doc_ids=doc, doc_sorted=doc_sorted))
 
 
 def tile_mask(table, block_size: int) -> MaskMod:
@@ -208,7 +218,7 @@ def and_masks(*mods: MaskMod) -> MaskMod:
 
     if any(s is None for s in specs):
         return mask
-    flags, left, right, doc, table, tblock = 0, -1, -1, None, None, 0
+    flags, left, right, doc, table, tblock, doc_sorted = 0, -1, -1, None, None, 0, False
     for s in specs:
         flags |= s.flags
         if s.flags & L.FA_MASK_WINDOW:
@@ -216,10 +226,10 @@ def and_masks(*mods: MaskMod) -> MaskMod:
         if s.doc_ids is not None:
             if doc is not None:
                 raise NotImplementedError("and_masks: at most one document mask")
-            doc = s.doc_ids
+            doc, doc_sorted = s.doc_ids, s.doc_sorted
         if s.tile_table is not None:
             if table is not None:
                 raise NotImplementedError("and_masks: at most one tile mask")
             table, tblock = s.tile_table, s.table_block
     return _with_spec(mask, MaskSpec(flags=flags, window_left=left, window_right=right, doc_ids=doc,
-                                     tile_table=table, table_block=tblock))
+                                     doc_sorted=doc_sorted, tile_table=table, table_block=tblock))

@@ -177,6 +177,33 @@ def test_document_and_tile_masks(D):
               O.and_(O.causal, O.tile_table(table, 128)))
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_document_id_layouts(D):
+    """Contiguous documents take the per-row interval path of the tcgen05 kernels (ids sorted),
+    interleaved ids the per-element path; per-batch document lengths give 2-D ids."""
+    T = 520
+    q, k, v, do = inputs((1, 2, T, D), (1, 2, T, D), torch.bfloat16, seed=11)
+    lens = [300, 20, 200]
+    doc = np.repeat(np.arange(3), lens)
+    check_all(q, k, v, do, pf.and_masks(pf.document_mask(lens), pf.sliding_window_mask(150, 0)),
+              O.and_(O.document(doc), O.sliding_window(150, 0)))
+    inter = (np.arange(T) // 37) % 3  # non-monotone ids: documents interleave
+    assert not pf.document_ids_mask(inter).__fa_spec__.doc_sorted
+    check_all(q, k, v, do, pf.and_masks(pf.document_ids_mask(inter), pf.causal_mask),
+              O.and_(O.document(inter), O.causal))
+    qb, kb, vb, dob = inputs((2, 2, T, D), (2, 2, T, D), torch.bfloat16, seed=12)
+    lens2 = [[100, 420], [260, 130, 130]]
+    mm = pf.and_masks(pf.document_mask(lens2), pf.causal_mask)
+    assert mm.__fa_spec__.doc_sorted and mm.__fa_spec__.depends_on_batch
+    o, g = run_api(qb, kb, vb, dob, mm)
+    for bi in range(2):
+        docb = np.repeat(np.arange(len(lens2[bi])), lens2[bi])
+        ro, _, rg = oracle(qb[bi:bi + 1], kb[bi:bi + 1], vb[bi:bi + 1], dob[bi:bi + 1], O.and_(O.document(docb), O.causal))
+        close("o", o[bi:bi + 1], ro, torch.bfloat16)
+        for n, a_, b_ in zip(("dq", "dk", "dv"), g, rg):
+            close(n, a_[bi:bi + 1], b_, torch.bfloat16)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("T", [1, 77, 200, 300, 129])
 def test_ragged_lengths(dtype, T):
