@@ -148,7 +148,7 @@ typedef struct {
 
 typedef struct {
   int32_t dtype;
-  int32_t B, H, H_kv;       /* H_kv must equal H for the backward pass in this build */
+  int32_t B, H, H_kv;       /* H_kv divides H; dk / dv have H_kv heads (sum over each group) */
   int32_t Tq, Tkv, D;
   FaTensor q, k, v, o, dout;
   FaTensor dq, dk, dv;

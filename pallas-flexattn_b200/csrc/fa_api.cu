@@ -194,7 +194,6 @@ static int check_bwd(const FaBwdParams* p) {
   if (!p) return fail(FA_ERR_INVALID, "params is NULL");
   int rc = check_common(p->dtype, p->B, p->H, p->H_kv, p->Tq, p->Tkv, p->D, p->blocks, p->mask, p->score);
   if (rc) return rc;
-  if (p->H_kv != p->H) return fail(FA_ERR_UNSUPPORTED, "backward with H_kv != H is not built");
   if ((rc = check_tensor(p->q, "q", 0)) || (rc = check_tensor(p->k, "k", 0)) || (rc = check_tensor(p->v, "v", 0)) ||
       (rc = check_tensor(p->o, "o", 0)) || (rc = check_tensor(p->dout, "dout", 0)) ||
       (rc = check_tensor(p->dq, "dq", 0)) || (rc = check_tensor(p->dk, "dk", 0)) || (rc = check_tensor(p->dv, "dv", 0)))
@@ -261,22 +260,22 @@ int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_str
   const bool tc_ok = p->dtype == FA_DTYPE_BF16 && (p->D == 64 || p->D == 128) && p->blocks.block_q == 128 &&
                      p->blocks.block_kv == 128 && tc_tensor_ok(p->q) && tc_tensor_ok(p->k) && tc_tensor_ok(p->v) &&
                      tc_tensor_ok(p->dout) && tc_tensor_ok(p->dk) && tc_tensor_ok(p->dv) &&
-                     bwd_tc_max_stages(p->D, p->blocks.nq) >= 1;
+                     bwd_tc_max_stages(p->D, p->blocks.nq, p->H / p->H_kv) >= 1;
   int kernel = p->kernel;
   if (kernel == FA_KERNEL_AUTO) kernel = tc_ok ? FA_KERNEL_TC : FA_KERNEL_SIMT;
   if (kernel == FA_KERNEL_TC) {
     if (!tc_ok)
       return fail(FA_ERR_UNSUPPORTED,
                   "tcgen05 backward needs bf16, D in {64,128}, 128x128 block tables and 16-byte aligned rows");
-    const int max_ns = bwd_tc_max_stages(p->D, p->blocks.nq);
+    const int max_ns = bwd_tc_max_stages(p->D, p->blocks.nq, p->H / p->H_kv);
     int ns = p->num_stages > 0 ? p->num_stages : 2;
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
     CUtensorMap tq, tk, tv, tdo, tdq;
     const int qrows = bwd_tc_q_rows(p->D);
     if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q", qrows)) ||
-        (rc = make_bf16_map(&tk, p->k, p->B, p->H, p->Tkv, p->D, "k")) ||
-        (rc = make_bf16_map(&tv, p->v, p->B, p->H, p->Tkv, p->D, "v")) ||
+        (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
+        (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")) ||
         (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout", qrows)) ||
         (rc = make_dq_accum_map(&tdq, a.dq_accum, p->B * p->H, p->Tq, p->D)))
       return rc;

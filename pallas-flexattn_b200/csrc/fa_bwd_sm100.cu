@@ -68,7 +68,7 @@ struct BwdSmemLayout {
       ent_off, total;
 };
 
-__host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int no_st, int nq) {
+__host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int no_st, int nq, int G) {
   const int QR = 128;
   BwdSmemLayout L;
   L.ktile = kBM * D * 2;
@@ -85,7 +85,7 @@ __host__ __device__ inline BwdSmemLayout bwd_smem_layout(int D, int nq_st, int n
   L.misc_off = L.bar_off + (2 * nq_st + 2 * no_st + 16) * 8;
   L.cls_off = L.misc_off + 16;
   L.ent_off = L.cls_off + 4 * nq;
-  L.total = L.ent_off + 4 * 2 * nq + 1024;  // entries: up to two q steps per 128-row q block
+  L.total = L.ent_off + 4 * nq * G + 1024;  // entries: one 128-row q step per q block and head
   return L;
 }
 
@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t IDESC_DQ = make_idesc_bf16(QR, D, 1, 1);   // dQ: A, B MN-major
 
   const int nq = a.bt.nq;
-  const BwdSmemLayout L = bwd_smem_layout(D, NQS, NOS, nq);
+  const int G = a.H / a.Hkv;  // query heads sharing this CTA's K/V head
+  const BwdSmemLayout L = bwd_smem_layout(D, NQS, NOS, nq, G);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + L.k_off;
@@ -135,9 +136,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   int* entries = reinterpret_cast<int*>(smem + L.ent_off);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x % (a.B * a.H);
-  const int j = blockIdx.x / (a.B * a.H);  // kv tile; low j first (the most q tiles under causal masks)
-  const int b = bh / a.H, h = bh % a.H;
+  // One CTA per (kv tile j, b, kv head hk); with grouped-query attention it walks the q
+  // tiles of all G query heads of the group, and dK/dV sum over them.
+  const int bhk = blockIdx.x % (a.B * a.Hkv);
+  const int j = blockIdx.x / (a.B * a.Hkv);  // kv tile; low j first (the most q tiles under causal masks)
+  const int b = bhk / a.Hkv, hk = bhk % a.Hkv;
   const int Tq_pad = (a.Tq + 127) / 128 * 128;
 
   if (warp == kWarpProd && lane == 0) {
@@ -172,6 +175,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tmem_alloc(tmem_base_s, 512);
     tmem_relinquish();
   }
+  int n_built = 0;  // entries built so far (producer warp)
+  for (int g = 0; g < G; ++g) {
+  const int h = hk * G + g;
   for (int i = tid; i < nq; i += kBwdThreads) cls[i] = 0;
   __syncthreads();
   {
@@ -189,10 +195,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   __syncthreads();
   if (warp == kWarpProd) {
-    // Step list: each listed 128-row q block becomes 128 / QR steps of QR rows (steps that
-    // start at or past Tq are dropped); entry = step index | class << 24 (1 partial, 2 full).
+    // Step list: each listed 128-row q block of head g becomes 128 / QR steps of QR rows
+    // (steps that start at or past Tq are dropped); entry = step | g << 16 | class << 24
+    // (class 1 partial, 2 full).
     constexpr int SPB = 128 / QR;
-    int base = 0;
+    int base = n_built;
     for (int i0 = 0; i0 < nq; i0 += 32) {
       const int i = i0 + lane;
       int c = (i < nq) ? cls[i] : 0;
@@ -206,11 +213,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      for (int s = 0; s < ns; ++s) entries[base + incl - ns + s] = (i * SPB + s) | (c << 24);
+      for (int s = 0; s < ns; ++s) entries[base + incl - ns + s] = (i * SPB + s) | (g << 16) | (c << 24);
       base += __shfl_sync(0xffffffffu, incl, 31);
     }
+    n_built = base;
     if (lane == 0) *n_entries_s = base;
   }
+  __syncthreads();
+  }  // heads of the group
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -224,15 +234,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (lane == 0 && n_ent > 0) {
         mbar_arrive_expect_tx(bar_kv, 2 * L.ktile);
         for (int c = 0; c < NCHUNK; ++c) {
-          tma_load_4d(sK + c * C::PANEL_K, &tm_k, bar_kv, c * 64, j * kBM, h, b);
-          tma_load_4d(sV + c * C::PANEL_K, &tm_v, bar_kv, c * 64, j * kBM, h, b);
+          tma_load_4d(sK + c * C::PANEL_K, &tm_k, bar_kv, c * 64, j * kBM, hk, b);
+          tma_load_4d(sV + c * C::PANEL_K, &tm_v, bar_kv, c * 64, j * kBM, hk, b);
         }
-        const float* lse2 = a.lse2 + (int64_t)bh * Tq_pad;
-        const float* dl = a.delta + (int64_t)bh * Tq_pad;
+        const float* lse2 = a.lse2 + (int64_t)b * a.H * Tq_pad;  // rows of head h at + h * Tq_pad
+        const float* dl = a.delta + (int64_t)b * a.H * Tq_pad;
         bool ok = true;
         int issued_q = 0, issued_o = 0;
         for (int t = 0; t < n_ent && ok; ++t) {
-          const int sub = entries[t] & 0xFFFFFF;
+          const int sub = entries[t] & 0xFFFF, h = hk * G + ((entries[t] >> 16) & 0xFF);
           const int qs = t % NQS, qu = t / NQS;
           if (!mbar_wait(bar_q_empty + qs, (qu & 1) ^ 1, abort_flag)) { ok = false; break; }
           // lse2 and delta ride with Q: the Q slot is released after dK(t), the last reader
@@ -240,8 +250,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mbar_arrive_expect_tx(bar_q_full + qs, L.qtile + 2 * QR * 4);
           for (int c = 0; c < NCHUNK; ++c)
             tma_load_4d(sQ + qs * L.qtile + c * C::PANEL_Q, &tm_q, bar_q_full + qs, c * 64, sub * QR, h, b);
-          bulk_load(sLse + qs * QR, lse2 + sub * QR, QR * 4, bar_q_full + qs);
-          bulk_load(sDl + qs * QR, dl + sub * QR, QR * 4, bar_q_full + qs);
+          bulk_load(sLse + qs * QR, lse2 + (int64_t)h * Tq_pad + sub * QR, QR * 4, bar_q_full + qs);
+          bulk_load(sDl + qs * QR, dl + (int64_t)h * Tq_pad + sub * QR, QR * 4, bar_q_full + qs);
           ++issued_q;
           const int os = t % NOS, ou = t / NOS;
           if (!mbar_wait(bar_o_empty + os, (ou & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -385,7 +395,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* stage = sDq + wq * kDqStage;
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
-      const int sub = entries[t] & 0xFFFFFF;
+      const int sub = entries[t] & 0xFFFF;
+      const int bh = b * a.H + hk * G + ((entries[t] >> 16) & 0xFF);  // dQ accumulator row block
       const int qb = C::DQ_OWN ? (t & 1) : 0;
       const uint32_t use = C::DQ_OWN ? (t >> 1) : t;  // completions of this buffer so far
       if (!(ok = mbar_wait(bar_dq_full + qb, use & 1, abort_flag))) break;
@@ -434,7 +445,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int kv = j * kBM + r;
     const int cbase = wg * NP;  // first q column (within the step) of this warpgroup
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
-    const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
+    int sc_head = hk * G;  // head the score context below belongs to
+    ScoreCtx sc = make_score_ctx(a.score, a.scale, sc_head, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
     const int kvg = kv + mc.kv_off;
     const float inv_cap_log2 = sc.inv_cap * kLn2;  // 1 / (cap * log2(e))
@@ -460,7 +472,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];
-      const int sub = e & 0xFFFFFF;
+      const int sub = e & 0xFFFF;
+      if (G > 1) {  // per-head score parameters (ALiBi slope, bias row)
+        const int h = hk * G + ((e >> 16) & 0xFF);
+        if (h != sc_head) {
+          sc_head = h;
+          sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
+        }
+      }
       const bool partial = ((e >> 24) & 3) == 1;
       const int qs = t % NQS;
       const uint32_t ph = t & 1;
@@ -575,9 +594,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
     }
     __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(a.dv.ptr) + (int64_t)b * a.dv.stride_b +
-                         (int64_t)h * a.dv.stride_h + (int64_t)kv * a.dv.stride_t;
+                         (int64_t)hk * a.dv.stride_h + (int64_t)kv * a.dv.stride_t;
     __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(a.dk.ptr) + (int64_t)b * a.dk.stride_b +
-                         (int64_t)h * a.dk.stride_h + (int64_t)kv * a.dk.stride_t;
+                         (int64_t)hk * a.dk.stride_h + (int64_t)kv * a.dk.stride_t;
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
       const float mul = which ? a.scale : 1.f;
@@ -615,10 +634,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-bool pick_stages(int D, int nq, int* nqs, int* nos) {
+bool pick_stages(int D, int nq, int G, int* nqs, int* nos) {
   const int cand[7][2] = {{4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}, {2, 1}, {0, 0}};
   for (int c = 0; cand[c][0]; ++c)
-    if (bwd_smem_layout(D, cand[c][0], cand[c][1], nq).total <= 227 * 1024) {
+    if (bwd_smem_layout(D, cand[c][0], cand[c][1], nq, G).total <= 227 * 1024) {
       *nqs = cand[c][0];
       *nos = cand[c][1];
       return true;
@@ -628,9 +647,9 @@ bool pick_stages(int D, int nq, int* nqs, int* nos) {
 
 }  // namespace
 
-int bwd_tc_max_stages(int D, int nq) {
+int bwd_tc_max_stages(int D, int nq, int G) {
   int a = 0, b = 0;
-  return pick_stages(D, nq, &a, &b) ? a : 0;
+  return pick_stages(D, nq, G, &a, &b) ? a : 0;
 }
 
 int bwd_tc_q_rows(int D) { return D == 128 ? BwdCfg<128>::QR : BwdCfg<64>::QR; }
@@ -638,11 +657,12 @@ int bwd_tc_q_rows(int D) { return D == 128 ? BwdCfg<128>::QR : BwdCfg<64>::QR; }
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream) {
   int nqs = 0, nos = 0;
-  if (!pick_stages(a.D, a.bt.nq, &nqs, &nos)) return cudaErrorInvalidValue;
+  const int G = a.H / a.Hkv;
+  if (!pick_stages(a.D, a.bt.nq, G, &nqs, &nos)) return cudaErrorInvalidValue;
   if (a.num_stages >= 2 && a.num_stages < nqs) nqs = a.num_stages;
   if (nos > nqs) nos = nqs;
-  const int smem = bwd_smem_layout(a.D, nqs, nos, a.bt.nq).total;
-  const dim3 grid((unsigned)(a.bt.nkv * a.B * a.H));
+  const int smem = bwd_smem_layout(a.D, nqs, nos, a.bt.nq, G).total;
+  const dim3 grid((unsigned)(a.bt.nkv * a.B * a.Hkv));
   const int sk = score_kind_of(a.score.flags);
   auto go = [&](auto kern, auto regs) -> cudaError_t {
     // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.

@@ -15,7 +15,7 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
                           cudaStream_t stream);
 
 // tcgen05 backward (fa_bwd_sm100.cu)
-int bwd_tc_max_stages(int D, int nq);
+int bwd_tc_max_stages(int D, int nq, int G);  // G = H / H_kv query heads per K/V head
 int bwd_tc_q_rows(int D);         // q rows per step (the Q / dO tensor-map box height)
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream);

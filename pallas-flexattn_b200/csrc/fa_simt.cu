@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dq_simt_kernel(const AttnArgs
   const int bq = a.bt.block_q, bkv = a.bt.block_kv;
   const int groups = (bq + kWarps - 1) / kWarps;
   const int qb = blockIdx.x / groups, grp = blockIdx.x % groups;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H, hk = h / (a.H / a.Hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int in_blk = grp * kWarps + warp;
   const int q_row = qb * bq + in_blk;
@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dq_simt_kernel(const AttnArgs
         const int r = idx / D, d = idx % D, kv = c0 + r;
         float kx = 0.f, vx = 0.f;
         if (kv < t_end) {
-          kx = to_f(row_ptr<T>(a.k, b, h, kv)[d]);
-          vx = to_f(row_ptr<T>(a.v, b, h, kv)[d]);
+          kx = to_f(row_ptr<T>(a.k, b, hk, kv)[d]);
+          vx = to_f(row_ptr<T>(a.v, b, hk, kv)[d]);
         }
         sK[r * DP + d] = kx;
         sV[r * DP + d] = vx;
@@ -292,29 +292,34 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dkv_simt_kernel(const AttnArg
   const int bq = a.bt.block_q, bkv = a.bt.block_kv;
   const int groups = (bkv + kWarps - 1) / kWarps;
   const int kb = blockIdx.x / groups, grp = blockIdx.x % groups;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  // One block per (kv block, b, kv head); dK and dV sum over the G = H / Hkv query heads of
+  // the group (grouped-query attention; G = 1 otherwise).
+  const int G = a.H / a.Hkv;
+  const int bhk = blockIdx.y, b = bhk / a.Hkv, hk = bhk % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int in_blk = grp * kWarps + warp;
   const int kv_row = kb * bkv + in_blk;
   const bool row_ok = in_blk < bkv && kv_row < a.Tkv;
 
-  const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
   const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
   if (row_ok) {
-    const T* k = row_ptr<T>(a.k, b, h, kv_row);
-    const T* v = row_ptr<T>(a.v, b, h, kv_row);
+    const T* k = row_ptr<T>(a.k, b, hk, kv_row);
+    const T* v = row_ptr<T>(a.v, b, hk, kv_row);
     for (int d = lane; d < D; d += 32) {
       sK[warp * D + d] = to_f(k[d]);
       sV[warp * D + d] = to_f(v[d]);
     }
   }
-  const int64_t tcol = table_head(a.bt, b, h) * a.bt.nkv + kb;
-  const RowList L =
-      row_list(a.bt.q_num_blocks, a.bt.q_indices, a.bt.full_q_num_blocks, a.bt.full_q_indices, tcol, a.bt.q_cap);
   float dk[kMaxDPerLane], dv[kMaxDPerLane];
 #pragma unroll
   for (int u = 0; u < kMaxDPerLane; ++u) dk[u] = dv[u] = 0.f;
 
+  for (int gi = 0; gi < G; ++gi) {
+  const int h = hk * G + gi, bh = b * a.H + h;
+  const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
+  const int64_t tcol = table_head(a.bt, b, h) * a.bt.nkv + kb;
+  const RowList L =
+      row_list(a.bt.q_num_blocks, a.bt.q_indices, a.bt.full_q_num_blocks, a.bt.full_q_indices, tcol, a.bt.q_cap);
   for (int e = 0; e < L.count(); ++e) {
     bool partial;
     const int i = L.at(e, &partial);
@@ -367,9 +372,10 @@ __global__ void __launch_bounds__(kWarps * 32) bwd_dkv_simt_kernel(const AttnArg
       }
     }
   }
+  }  // heads of the group
   if (!row_ok) return;
-  T* dkr = row_ptr_w<T>(a.dk, b, h, kv_row);
-  T* dvr = row_ptr_w<T>(a.dv, b, h, kv_row);
+  T* dkr = row_ptr_w<T>(a.dk, b, hk, kv_row);
+  T* dvr = row_ptr_w<T>(a.dv, b, hk, kv_row);
 #pragma unroll
   for (int u = 0; u < kMaxDPerLane; ++u) {
     const int d = lane + 32 * u;
@@ -408,7 +414,7 @@ cudaError_t launch_bwd_simt(const AttnArgs& a, int dtype, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
   }
   const int groups = (a.bt.block_kv + kWarps - 1) / kWarps;
-  const dim3 grid((unsigned)(a.bt.nkv * groups), (unsigned)(a.B * a.H));
+  const dim3 grid((unsigned)(a.bt.nkv * groups), (unsigned)(a.B * a.Hkv));
   const size_t smem = (size_t)(2 * kChunk * (a.D + 1) + 2 * kWarps * a.D + 3 * kChunk) * sizeof(float);
   return dtype == FA_DTYPE_F32 ? launch_simt(bwd_dkv_simt_kernel<float>, grid, smem, stream, a)
                                : launch_simt(bwd_dkv_simt_kernel<__nv_bfloat16>, grid, smem, stream, a);

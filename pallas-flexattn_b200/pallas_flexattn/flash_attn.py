@@ -127,8 +127,6 @@ class _Plan:
             raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
         if H % Hkv:
             raise ValueError(f"H={H} must be a multiple of the K/V heads {Hkv}")
-        if need_bwd and Hkv != H:
-            raise NotImplementedError("backward with fewer K/V heads than Q heads is not built")
         if D % 8 or D > 256:
             raise NotImplementedError(f"head dim {D}: need a multiple of 8 up to 256")
         self.device = q.device

@@ -219,15 +219,24 @@ def test_cross_attention_lengths(dtype):
     check_all(q, k, v, do, None, None)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("D", [64, 128])
-def test_grouped_query_forward(D):
-    q, k, v, do = inputs((2, 8, 256, D), (2, 2, 256, D), torch.bfloat16, seed=12)
-    o, _ = run_api(q, k, v, do, pf.causal_mask, bwd=False)
-    kr, vr = k.repeat_interleave(4, dim=1), v.repeat_interleave(4, dim=1)
-    ro, _, _ = oracle(q, kr, vr, do, O.causal)
-    close("o", o, ro, torch.bfloat16)
-    with pytest.raises(NotImplementedError):
-        run_api(q, k, v, do, pf.causal_mask, bwd=True)
+@pytest.mark.parametrize("Hkv", [1, 2])
+def test_grouped_query_attention(dtype, D, Hkv):
+    """GQA / MQA: 8 query heads share Hkv K/V heads; dK, dV sum over each group (the oracle
+    runs on K/V repeated per query head and its gradients are summed back)."""
+    G = 8 // Hkv
+    q, k, v, do = inputs((2, 8, 300, D), (2, Hkv, 300, D), dtype, seed=12 + Hkv)
+    al = pf.alibi_score_mod(8)
+    o, (dq, dk, dv) = run_api(q, k, v, do, pf.causal_mask, al)
+    kr, vr = k.repeat_interleave(G, dim=1), v.repeat_interleave(G, dim=1)
+    ro, _, (rdq, rdk, rdv) = oracle(q, kr, vr, do, O.causal, (O.alibi(pf.alibi_slopes(8).numpy()),))
+    close("o", o, ro, dtype)
+    close("dq", dq, rdq, dtype)
+    rdk = rdk.reshape(2, Hkv, G, 300, D).sum(axis=2)
+    rdv = rdv.reshape(2, Hkv, G, 300, D).sum(axis=2)
+    close("dk", dk, rdk, dtype)
+    close("dv", dv, rdv, dtype)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
