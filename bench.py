@@ -35,6 +35,7 @@ import threading
 import time
 from datetime import timedelta
 from pathlib import Path
+from typing import Optional
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "pallas-flexattn_b200"))
@@ -205,6 +206,42 @@ def parity_check(w, q, k, v, do) -> dict:
         ok = ok and excess <= 0 and rel <= 5e-3
     res["slice"] = "b=0, h=0 of the timed inputs"
     res["pass"] = ok
+    return res
+
+
+def sdpa_comparators(w, q, k, v, do, flops: float, steps: int = 20) -> Optional[dict]:
+    """torch scaled_dot_product_attention (cuDNN and flash backends) on the same causal
+    shapes, forward + backward, for context only (the reference benchmark's comparators);
+    None for workloads that SDPA cannot express (score_mod, sparse masks)."""
+    import pallas_flexattn as pf
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    if w.mask_mod is not pf.causal_mask or w.score_mod is not None or w.dtype != torch.bfloat16:
+        return None
+    res = {}
+    for name, backend in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION),
+                          ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+        try:
+            qq, kk, vv = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+
+            def step():
+                with sdpa_kernel(backend):
+                    o = torch.nn.functional.scaled_dot_product_attention(qq, kk, vv, is_causal=True)
+                torch.autograd.grad(o, (qq, kk, vv), do)
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            for _ in range(steps):
+                step()
+            e_ev.record()
+            torch.cuda.synchronize()
+            ms = s_ev.elapsed_time(e_ev) / steps
+            res[name] = {"ms_per_step": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+        except Exception as e:  # backend not built for this GPU / shape
+            res[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:100]}"}
     return res
 
 
@@ -427,6 +464,7 @@ def main():
 
     parity = parity_check(w, q, k, v, do)
     bm_ms = block_mask_ms(w, device)
+    comparators = sdpa_comparators(w, q, k, v, do, fwd_flops + bwd_flops) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, n_pairs)
@@ -457,6 +495,7 @@ def main():
             "gpu_launches": args.steps * (fwd_launches + bwd_launches),
             "parity": parity,
             "block_mask_ms": bm_ms,
+            "comparators": comparators,
             "unmasked_pairs_per_bh": n_pairs,
         }
         print(json.dumps(line), flush=True)
