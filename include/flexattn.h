@@ -18,6 +18,7 @@
  *   fa_create_block_mask <- create_block_mask           src/pallas_flexattn/block_mask.py:54-129
  *   fa_block_tables_from_lists <- BlockMask fields      src/pallas_flexattn/block_mask.py:16-51
  *   fa_lse_merge         <- (no counterpart; combine step of the context-parallel ring)
+ *   fa_decode            <- (no counterpart; split-KV decode against a K/V cache)
  */
 #ifndef FLEXATTN_H_
 #define FLEXATTN_H_
@@ -230,6 +231,33 @@ FA_API int fa_block_tables_from_lists(int32_t num_b, int32_t nq, int32_t nkv, co
  * o_acc is fp32 [rows, D]; o_part is dtype [rows, D] with row stride o_part_stride. */
 FA_API int fa_lse_merge(int32_t rows, int32_t D, float* o_acc, float* lse_acc, const void* o_part,
                  int64_t o_part_stride, int32_t o_part_dtype, const float* lse_part, fa_stream_t stream);
+
+/* ------------------------------------------------------------------ decode (split-KV)
+ * Attention of a few new query tokens per sequence against a K/V cache.  Batch b holds
+ * kv_lens[b] valid cache positions (all Tkv when kv_lens is NULL); its Tq query rows are
+ * the last Tq positions of that sequence: row i sits at global position
+ * kv_lens[b] - Tq + i, which the mask and score mods see (causal = keys up to the row's
+ * own position).  The cache is cut into num_splits chunks handled by separate CTAs (one
+ * per chunk, batch and K/V head, covering every query head of the group), and a second
+ * kernel merges the chunks' (o, lse).  Supported: D in {64, 128, 256}, H / H_kv * Tq <= 64,
+ * mask flags CAUSAL / WINDOW, score flags ALIBI / SOFTCAP.  No counterpart in the
+ * reference. */
+typedef struct {
+  int32_t dtype;            /* FA_DTYPE_BF16 or FA_DTYPE_F32 */
+  int32_t B, H, H_kv, Tq, Tkv, D;
+  FaTensor q, k, v, o;      /* q, o [B, H, Tq, D]; k, v [B, H_kv, Tkv, D] (the cache) */
+  float* lse;               /* [B, H, Tq] fp32 natural-log logsumexp */
+  const int32_t* kv_lens;   /* [B] device int32 valid cache lengths (Tq <= len <= Tkv), or NULL */
+  float scale;
+  FaMaskSpec mask;          /* q_offset / kv_offset must be 0 (positions come from kv_lens) */
+  FaScoreSpec score;
+  int32_t num_splits;       /* cache chunks per (b, K/V head); 0 = chosen from the shape */
+  int32_t* status;          /* optional, as in FaFwdParams */
+} FaDecodeParams;
+
+/* Bytes of device workspace fa_decode needs (the chunks' partial o and lse). */
+FA_API int fa_decode_workspace_size(const FaDecodeParams* p, size_t* bytes);
+FA_API int fa_decode(const FaDecodeParams* p, void* workspace, size_t workspace_bytes, fa_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -10,6 +10,10 @@ novastar53/pallas-flexattn (paths inside that project):
 * ``mha_reference``             flash_attn.py:45-56 (materialised softmax attention),
                                 extended with FlexAttention's score_mod, applied to the
                                 scaled logit before the mask;
+* ``decode_reference``          the same formula for the last Tq positions of each
+                                sequence against a K/V cache of per-batch length
+                                (no counterpart in the reference; checked against
+                                mha_reference);
 * ``flash_fwd_tiled``           flash_attn.py:59-108 (online-softmax tile recurrence,
                                 including its NaN->0 guards at :92 and :96);
 * ``attention_bwd``             flash_attn.py:168-173 (delta), :241-245 (dK/dV),
@@ -163,6 +167,49 @@ def mha_reference(q, k, v, mask: Optional[Callable] = None, score_mods=(), scale
     if empty_rows_zero:
         o = np.where(empty, 0.0, o)
         lse = np.where(empty[..., 0], -np.inf, lse)
+    return o, lse
+
+
+def decode_reference(q, k, v, kv_lens=None, mask: Optional[Callable] = None, score_mods=(), scale=None,
+                     dtype=np.float64):
+    """Decode against a K/V cache: q [B, H, Tq, D], k / v [B, H_kv, Tkv, D] with H_kv | H.
+
+    Batch b keeps its first kv_lens[b] cache rows (all Tkv when kv_lens is None); query row i
+    sits at global position kv_lens[b] - Tq + i, so it is the last Tq rows of
+    mha_reference (flash_attn.py:45-56) over that sequence, with each K/V head shared by
+    H / H_kv consecutive query heads.  Rows with no visible key give o = 0, lse = -inf.
+    Returns (o, lse).
+    """
+    B, H, Tq, D = q.shape
+    Hkv, Tkv = k.shape[1], k.shape[2]
+    G = H // Hkv
+    s = 1.0 / math.sqrt(D) if scale is None else scale
+    o = np.zeros((B, H, Tq, D), dtype)
+    lse = np.full((B, H, Tq), -np.inf, dtype)
+    for b in range(B):
+        n = Tkv if kv_lens is None else int(kv_lens[b])
+        qi = (np.arange(Tq) + n - Tq)[:, None]
+        ki = np.arange(n)[None, :]
+        kb = np.repeat(k[b, :, :n].astype(dtype), G, axis=0)
+        vb = np.repeat(v[b, :, :n].astype(dtype), G, axis=0)
+        x = np.einsum("hqd,hkd->hqk", q[b].astype(dtype), kb) * s
+        h = np.arange(H)[:, None, None]
+        for f in score_mods:
+            x = f(x, h, qi, ki)
+        if mask is not None:
+            x = np.where(mask(qi, ki), x, -np.inf)
+        if n == 0:
+            continue
+        m = x.max(axis=-1, keepdims=True)
+        empty = ~np.isfinite(m)
+        m_safe = np.where(empty, 0.0, m)
+        p = np.exp(x - m_safe)
+        l = p.sum(axis=-1, keepdims=True)
+        with np.errstate(invalid="ignore", divide="ignore"):
+            ob = np.einsum("hqk,hkd->hqd", p / l, vb)
+            lb = (m_safe + np.log(l))[..., 0]
+        o[b] = np.where(empty, 0.0, ob)
+        lse[b] = np.where(empty[..., 0], -np.inf, lb)
     return o, lse
 
 

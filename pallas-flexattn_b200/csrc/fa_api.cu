@@ -138,6 +138,24 @@ AttnArgs base_args(int B, int H, int Hkv, int Tq, int Tkv, int D, float scale, c
 // Sets the thread's fa_last_error message from another translation unit; returns `code`.
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+int make_row_tile_map(CUtensorMap* map, const FaTensor& t, int dtype, int B, int heads, int T, int D, int box_rows,
+                      const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int es = dtype == FA_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(t.ptr) || (t.stride_t * es) % 16 || (t.stride_h * es) % 16 || (t.stride_b * es) % 16)
+    return fail(FA_ERR_INVALID, "%s: base address and strides must be multiples of 16 bytes", name);
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)heads, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)t.stride_t * es, (cuuint64_t)t.stride_h * es, (cuuint64_t)t.stride_b * es};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.ptr, dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ERR_INVALID, "tensor map for %s rejected (CUresult %d)", name, (int)r);
+  return FA_OK;
+}
+
 }  // namespace fa
 
 using namespace fa;

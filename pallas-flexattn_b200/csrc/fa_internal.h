@@ -8,6 +8,10 @@
 namespace fa {
 
 int set_last_error(int code, const char* msg);
+// 4-D tensor map over a [B, heads, T, D] tensor (bf16 or fp32): box = one 128-byte panel of
+// columns x box_rows rows, 128-byte swizzle.  Rejects misaligned bases and strides.
+int make_row_tile_map(CUtensorMap* map, const FaTensor& t, int dtype, int B, int heads, int T, int D, int box_rows,
+                      const char* name);
 
 // tcgen05 forward (fa_fwd_sm100.cu)
 int fwd_tc_max_stages(int D, int nkv);

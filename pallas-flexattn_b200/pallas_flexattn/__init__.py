@@ -12,6 +12,7 @@ from .flash_attn import (
     flash_attention_fwd,
     mha_reference,
 )
+from .decode import flash_attention_decode
 from .mask_mod import (
     MaskMod,
     and_masks,
@@ -46,6 +47,7 @@ __all__ = [
     "flash_attention",
     "flash_attention_fwd",
     "flash_attention_bwd",
+    "flash_attention_decode",
     "mha_reference",
     "MaskMod",
     "causal_mask",

@@ -132,6 +132,29 @@ class FaBwdParams(C.Structure):
     ]
 
 
+class FaDecodeParams(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int32),
+        ("B", C.c_int32),
+        ("H", C.c_int32),
+        ("H_kv", C.c_int32),
+        ("Tq", C.c_int32),
+        ("Tkv", C.c_int32),
+        ("D", C.c_int32),
+        ("q", FaTensor),
+        ("k", FaTensor),
+        ("v", FaTensor),
+        ("o", FaTensor),
+        ("lse", C.c_void_p),
+        ("kv_lens", C.c_void_p),
+        ("scale", C.c_float),
+        ("mask", FaMaskSpec),
+        ("score", FaScoreSpec),
+        ("num_splits", C.c_int32),
+        ("status", C.c_void_p),
+    ]
+
+
 class FaBlockMaskOut(C.Structure):
     _fields_ = [
         ("num_b", C.c_int32),
@@ -168,6 +191,8 @@ EXPORTS = {
         [C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
          C.POINTER(FaBlockMaskOut), C.c_void_p],
     ),
+    "fa_decode_workspace_size": (C.c_int, [C.POINTER(FaDecodeParams), C.POINTER(C.c_size_t)]),
+    "fa_decode": (C.c_int, [C.POINTER(FaDecodeParams), C.c_void_p, C.c_size_t, C.c_void_p]),
     "fa_lse_merge": (
         C.c_int,
         [C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p],

@@ -13,7 +13,8 @@ from pallas_flexattn import _lib as L
 
 REPO = Path(__file__).resolve().parent.parent
 HEADER = REPO / "include" / "flexattn.h"
-STRUCTS = ["FaMaskSpec", "FaScoreSpec", "FaBlockTables", "FaTensor", "FaFwdParams", "FaBwdParams", "FaBlockMaskOut"]
+STRUCTS = ["FaMaskSpec", "FaScoreSpec", "FaBlockTables", "FaTensor", "FaFwdParams", "FaBwdParams", "FaDecodeParams",
+           "FaBlockMaskOut"]
 
 
 def declared_functions():
@@ -48,6 +49,38 @@ def test_error_path_without_gpu():
     bp.B, bp.H, bp.H_kv, bp.Tq, bp.Tkv, bp.D = 1, 16, 16, 8192, 8192, 128
     assert L.lib().fa_bwd_noalloc(C.byref(bp), None) == L.FA_ERR_UNSUPPORTED
     assert b"static scratch" in L.lib().fa_last_error()
+
+
+def test_decode_validation_without_gpu():
+    """fa_decode rejects unsupported requests before any CUDA call; the workspace size is
+    a pure function of the shape (splits x rows x (D + 1) floats)."""
+    lib = L.lib()
+    dp = L.FaDecodeParams()
+    dp.dtype, dp.B, dp.H, dp.H_kv, dp.Tq, dp.Tkv, dp.D = L.FA_DTYPE_BF16, 2, 8, 2, 1, 4096, 128
+    size = C.c_size_t(0)
+    assert lib.fa_decode_workspace_size(C.byref(dp), C.byref(size)) == 0
+    rows = 2 * 8 * 1
+    assert size.value >= rows * 129 * 4 and (size.value - 256) % (rows * 129 * 4) == 0
+    dp.num_splits = 3
+    assert lib.fa_decode_workspace_size(C.byref(dp), C.byref(size)) == 0
+    assert size.value == 3 * rows * 129 * 4 + 256
+    for field, value, code, text in [("D", 96, L.FA_ERR_UNSUPPORTED, b"head dim"),
+                                     ("Tq", 17, L.FA_ERR_UNSUPPORTED, b"query rows"),
+                                     ("H_kv", 3, L.FA_ERR_INVALID, b"multiple"),
+                                     ("Tkv", 0, L.FA_ERR_INVALID, b"shape")]:
+        bad = L.FaDecodeParams.from_buffer_copy(dp)
+        setattr(bad, field, value)
+        assert lib.fa_decode_workspace_size(C.byref(bad), C.byref(size)) == code, field
+        assert text in lib.fa_last_error(), (field, lib.fa_last_error())
+    bad = L.FaDecodeParams.from_buffer_copy(dp)
+    bad.mask.flags = L.FA_MASK_DOCUMENT
+    assert lib.fa_decode_workspace_size(C.byref(bad), C.byref(size)) == L.FA_ERR_UNSUPPORTED
+    bad = L.FaDecodeParams.from_buffer_copy(dp)
+    bad.mask.q_offset = 4
+    assert lib.fa_decode_workspace_size(C.byref(bad), C.byref(size)) == L.FA_ERR_INVALID
+    # NULL tensors are caught by fa_decode itself (before the workspace check)
+    assert lib.fa_decode(C.byref(dp), None, 0, None) == L.FA_ERR_INVALID
+    assert b"NULL" in lib.fa_last_error()
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")

@@ -150,6 +150,26 @@ def test_fully_masked_rows_follow_flexattention_convention():
     assert np.all(dq[0, 0, :4] == 0) and np.isfinite(dq).all() and np.isfinite(dk).all()
 
 
+@pytest.mark.parametrize("mask_name", ["none", "causal", "window"])
+def test_decode_reference_is_the_tail_of_full_attention(mask_name):
+    """decode_reference for batch b equals the last Tq rows of mha_reference over that
+    sequence's first kv_lens[b] positions, with grouped K/V heads expanded."""
+    rng = np.random.default_rng(11)
+    B, H, Hkv, Tq, Tkv, D = 3, 4, 2, 3, 40, 8
+    lens = [40, 17, 3]
+    q_full = rng.standard_normal((B, H, Tkv, D))
+    k, v = (rng.standard_normal((B, Hkv, Tkv, D)) for _ in range(2))
+    mask = {"none": None, "causal": O.causal, "window": O.and_(O.causal, O.sliding_window(5, 0))}[mask_name]
+    mods = (O.alibi(O.alibi_slopes(H)), O.softcap(20.0))
+    q = np.stack([q_full[b, :, n - Tq:n] for b, n in enumerate(lens)])
+    o, lse = O.decode_reference(q, k, v, lens, mask, mods)
+    for b, n in enumerate(lens):
+        kk, vv = (np.repeat(x[b:b + 1, :, :n], H // Hkv, axis=1) for x in (k, v))
+        ro, rl = O.mha_reference(q_full[b:b + 1, :, :n], kk, vv, mask, mods)
+        np.testing.assert_allclose(o[b], ro[0, :, n - Tq:], atol=1e-12)
+        np.testing.assert_allclose(lse[b], rl[0, :, n - Tq:], atol=1e-12)
+
+
 # Exact classification on the benchmark masks: tile counts (full, partial).
 EXACT_COUNTS = {
     "cfg1_causal_T512_b128": (6, 4),
