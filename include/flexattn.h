@@ -239,7 +239,8 @@ FA_API int fa_lse_merge(int32_t rows, int32_t D, float* o_acc, float* lse_acc, c
  * kv_lens[b] - Tq + i, which the mask and score mods see (causal = keys up to the row's
  * own position).  The cache is cut into num_splits chunks handled by separate CTAs (one
  * per chunk, batch and K/V head, covering every query head of the group), and a second
- * kernel merges the chunks' (o, lse).  Supported: D in {64, 128, 256}, H / H_kv * Tq <= 64,
+ * kernel merges the chunks' (o, lse).  bf16 runs on the tensor cores (tcgen05), fp32 on
+ * CUDA cores.  Supported: D in {64, 128, 256}, H / H_kv * Tq <= 128 (bf16) or <= 64 (fp32),
  * mask flags CAUSAL / WINDOW, score flags ALIBI / SOFTCAP.  No counterpart in the
  * reference. */
 typedef struct {

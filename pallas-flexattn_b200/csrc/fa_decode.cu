@@ -9,10 +9,12 @@
 // Per CTA: TMA streams 64-row K and V tiles (128-byte swizzled panels) through a ring of
 // stages guarded by mbarriers; the 256 threads then run, per tile,
 //   scores   thread = (cache row j, every 4th query row): 16-byte K chunks against fp32 Q
-//            (the swizzle spreads the 32 rows a warp reads over all banks),
+//            (the swizzle spreads the 32 rows a warp reads over all banks); with one or
+//            two query rows the threads split the head dimension instead,
 //   softmax  warp = query row, online (running max and sum per row),
 //   P V      thread = (8 output columns, every RG-th query row), fp32 accumulators in
-//            registers, probabilities read 4 cache rows at a time,
+//            registers, probabilities read 4 cache rows at a time; with fewer query rows
+//            than RG the threads also split the tile's cache rows (partials added at the end),
 // and thread 0 refills the stage.  Each CTA writes its normalised partial (o, lse) to the
 // workspace; decode_merge_kernel combines the chunks by log-sum-exp.  Query row i of batch b
 // sits at global position kv_lens[b] - Tq + i.
@@ -20,6 +22,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 
 #include "fa_common.cuh"
@@ -32,7 +36,8 @@ namespace {
 
 constexpr int kDecThreads = 256;
 constexpr int kDecKT = 64;          // cache rows per tile (the TMA box height)
-constexpr int kDecMaxRows = 64;     // G * Tq
+constexpr int kDecMaxRows = 64;     // G * Tq, CUDA-core kernel (fp32)
+constexpr int kDecMaxRowsTc = 128;  // G * Tq, tcgen05 kernel (bf16)
 constexpr int kDecPS = kDecKT + 4;  // row stride of the score tile in floats (16-byte aligned, bank-shifted)
 constexpr int kPanelBytes = kDecKT * 128;
 
@@ -57,7 +62,6 @@ inline size_t decode_smem_bytes(int D, int es, int M, int stages) {
 }
 
 __device__ __forceinline__ float dec_ld(const float* p) { return *p; }
-__device__ __forceinline__ float dec_ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 // Element values of one 16-byte chunk.
 __device__ __forceinline__ void unpack_chunk(const uint4 raw, float (&f)[4]) {
@@ -152,8 +156,20 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
   const float cap = softcap ? a.score.softcap : 1.f, inv_cap = 1.f / cap;
   const int mflags = a.mask.flags, left = a.mask.window_left, right = a.mask.window_right;
 
-  const int cg = tid % NCG, rg = tid / NCG;          // P V phase
-  const int jrow = tid % kDecKT, mg = tid / kDecKT;  // score phase
+  // score phase: thread = (cache row jrow, row group mg); with M = 1 or 2 the groups split the
+  // head dimension into DS parts instead, leaving MG = 4 / DS row groups
+  const int jrow = tid % kDecKT, mg = tid / kDecKT;
+  const int DS = M == 1 ? 4 : (M == 2 ? 2 : 1), MG = 4 / DS, ds = mg % DS, mq = mg / DS;
+  // P V phase: thread = (column group cg, slot rg); with fewer rows than slots the slots also
+  // split the tile's cache rows into JG groups (partial sums added at the end)
+  const int cg = tid % NCG, rg = tid / NCG;
+  int JG = 1;
+  {
+    int m2 = 1;
+    while (m2 < M) m2 <<= 1;
+    if (m2 < RG) JG = min(16, RG / m2);
+  }
+  const int RS = RG / JG, jg = rg / RS, mrow = rg % RS, jlen = kDecKT / JG;
   float acc[RPT][8];
 #pragma unroll
   for (int r = 0; r < RPT; ++r)
@@ -177,18 +193,21 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
       __syncthreads();
     }
 
-    // ---- scores (log2 domain), masked to -inf
+    // ---- scores (log2 domain), masked to -inf.  With M < 4 the four row groups split the
+    //      head dimension instead (DS parts); part ds > 0 leaves its partial dot product in
+    //      score row ds * M + m for part 0 to add.
     {
+      const int c0 = ds * (CHUNKS / DS), c1 = c0 + CHUNKS / DS;
       float dot[SPT];
 #pragma unroll
       for (int r = 0; r < SPT; ++r) dot[r] = 0.f;
 #pragma unroll 2
-      for (int c = 0; c < CHUNKS; ++c) {
+      for (int c = c0; c < c1; ++c) {
         float kf[EPC];
         unpack_chunk(*reinterpret_cast<const uint4*>(kst + chunk_off(jrow, c)), kf);
 #pragma unroll
         for (int r = 0; r < SPT; ++r) {
-          const int m = mg + 4 * r;
+          const int m = mq + MG * r;
           if (m < M) {
             const float4* q4 = reinterpret_cast<const float4*>(sQ + m * D + c * EPC);
 #pragma unroll
@@ -202,21 +221,29 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
           }
         }
       }
-      const int kvpos = t0 + jrow;
+      if (DS > 1) {
+        if (ds > 0 && mq < M) sP[(ds * M + mq) * kDecPS + jrow] = dot[0];
+        __syncthreads();
+        if (ds == 0 && mq < M)
+          for (int d2 = 1; d2 < DS; ++d2) dot[0] += sP[(d2 * M + mq) * kDecPS + jrow];
+      }
+      if (ds == 0) {
+        const int kvpos = t0 + jrow;
 #pragma unroll
-      for (int r = 0; r < SPT; ++r) {
-        const int m = mg + 4 * r;
-        if (m >= M) continue;
-        const int qpos = qbase + m % a.Tq;
-        float x = fmaf(sSlope[m], (float)(kvpos - qpos), dot[r]);
-        if (softcap) x = cap * fast_tanh(x * inv_cap);
-        bool keep = jrow < n;
-        if (mflags & FA_MASK_CAUSAL) keep = keep && kvpos <= qpos;
-        if (mflags & FA_MASK_WINDOW) {
-          if (left >= 0) keep = keep && qpos - kvpos <= left;
-          if (right >= 0) keep = keep && kvpos - qpos <= right;
+        for (int r = 0; r < SPT; ++r) {
+          const int m = mq + MG * r;
+          if (m >= M) continue;
+          const int qpos = qbase + m % a.Tq;
+          float x = fmaf(sSlope[m], (float)(kvpos - qpos), dot[r]);
+          if (softcap) x = cap * fast_tanh(x * inv_cap);
+          bool keep = jrow < n;
+          if (mflags & FA_MASK_CAUSAL) keep = keep && kvpos <= qpos;
+          if (mflags & FA_MASK_WINDOW) {
+            if (left >= 0) keep = keep && qpos - kvpos <= left;
+            if (right >= 0) keep = keep && kvpos - qpos <= right;
+          }
+          sP[m * kDecPS + jrow] = keep ? x * kLog2e : -INFINITY;
         }
-        sP[m * kDecPS + jrow] = keep ? x * kLog2e : -INFINITY;
       }
     }
     __syncthreads();
@@ -242,21 +269,22 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
       }
     }
     __syncthreads();
-    // ---- P V over the tile's first n rows, rounded up to 4 (the rows past n are zero)
+    // ---- P V over this thread's share of the tile's first n rows, rounded up to 4 (the rows
+    //      past n are zero)
 #pragma unroll
     for (int r = 0; r < RPT; ++r) {
-      const int m = rg + RG * r;
+      const int m = mrow + RS * r;
       if (m < M) {
         const float al = sAlpha[m];
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[r][e] *= al;
       }
     }
-    for (int j0 = 0; j0 < n; j0 += 4) {
+    for (int j0 = jg * jlen, j1 = min(j0 + jlen, n); j0 < j1; j0 += 4) {
       float4 p4[RPT];
 #pragma unroll
       for (int r = 0; r < RPT; ++r) {
-        const int m = rg + RG * r;
+        const int m = mrow + RS * r;
         p4[r] = m < M ? *reinterpret_cast<const float4*>(sP + m * kDecPS + j0) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
@@ -298,12 +326,29 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
     __syncthreads();
     return;
   }
+  if (JG > 1) {  // add the row groups' partial sums (row mrow only: RS >= M); the stages are free now
+    float* red = reinterpret_cast<float*>(base);  // [JG][RS][D]
+    __syncthreads();
+    if (mrow < M) {
+      float4* dst = reinterpret_cast<float4*>(red + (jg * RS + mrow) * D + cg * 8);
+      dst[0] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+      dst[1] = make_float4(acc[0][4], acc[0][5], acc[0][6], acc[0][7]);
+    }
+    __syncthreads();
+    if (jg == 0 && mrow < M)
+      for (int g2 = 1; g2 < JG; ++g2) {
+        const float4* src = reinterpret_cast<const float4*>(red + (g2 * RS + mrow) * D + cg * 8);
+        const float4 lo = src[0], hi = src[1];
+        acc[0][0] += lo.x; acc[0][1] += lo.y; acc[0][2] += lo.z; acc[0][3] += lo.w;
+        acc[0][4] += hi.x; acc[0][5] += hi.y; acc[0][6] += hi.z; acc[0][7] += hi.w;
+      }
+  }
   // ---- this chunk's normalised partial (o, lse); an empty chunk gives o = 0, lse = -inf
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
 #pragma unroll
   for (int r = 0; r < RPT; ++r) {
-    const int m = rg + RG * r;
-    if (m >= M) continue;
+    const int m = mrow + RS * r;
+    if (m >= M || jg != 0) continue;
     const int g = m / a.Tq, i = m % a.Tq;
     const int64_t row = ((int64_t)b * a.H + hk * a.G + g) * a.Tq + i;
     const float l = sSum[m], inv = l > 0.f ? 1.f / l : 0.f;
@@ -314,39 +359,390 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
   }
 }
 
-// One warp per output row: log-sum-exp merge of the chunks' partials into o and lse.
-template <typename T>
+// ---------------------------------------------------------------------------------------------
+// tcgen05 split kernel (bf16).  The query rows of the group (M <= 128, zero-padded to 128) are
+// the MMA's M dimension and the 64-row cache tile its N:
+//   S = Q K^T   (kind::f16, M = 128, N = 64, K = D; Q and K from shared memory) into one of two
+//               TMEM score buffers, so the next tile's S is computed during this tile's softmax,
+//   P = exp2(S - m) by the warps that own the rows (thread = row, as in the forward kernel),
+//               written back over S in TMEM as bf16,
+//   O += P V    (A = P from TMEM, B = V from shared memory, MN-major; N = D).
+// The padded rows cost tensor-core time only, of which decode has plenty: a tile's HBM bytes
+// take longer than its MMAs.  Warps: ceil(M / 32) softmax warps (those whose TMEM lanes hold
+// real rows; warp 0 also issues the MMAs) and one producer warp that streams K/V tiles
+// through the stage ring, refilling a stage as soon as the PV MMA that read it completes
+// (per-stage empty barriers committed by the MMA issuer).  The row max used for P moves only
+// when a tile's max exceeds it by more than 8 (log2 units): O is rescaled rarely and P <= 256.
+constexpr float kDecRescaleThreshold = 8.f;
+
+__host__ __device__ constexpr uint32_t decode_tc_tmem_cols(int D) { return D <= 128 ? 256u : 512u; }
+
+// Dynamic shared memory of the tcgen05 kernel: K/V stages, the 128-row Q operand, barriers.
+inline size_t decode_tc_smem_bytes(int D, int stages) {
+  return 1024 + (size_t)stages * 2 * kDecKT * D * 2 + (size_t)128 * D * 2 + 256;
+}
+
+__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "barrier.cta.red.or.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(nthreads), "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_sync_n(int id, int nthreads) {
+  asm volatile("barrier.cta.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ CUtensorMap tk,
+                                                        const __grid_constant__ CUtensorMap tv, const DecodeArgs a) {
+  constexpr int TILE = kDecKT * D * 2;  // bytes of a 64-row K or V tile
+  constexpr int QPANEL = 128 * 128;     // bytes of one 64-column panel of the 128-row Q operand
+  constexpr int NPANEL = D / 64;
+  constexpr uint32_t TM_COLS = decode_tc_tmem_cols(D);
+  constexpr uint32_t TM_S = 0, TM_O = 2 * kDecKT;  // S buffers at 0 and 64 (fp32; P over them as bf16), O
+  constexpr uint32_t IDESC_S = make_idesc_bf16(128, kDecKT, 0, 0);
+  constexpr uint32_t IDESC_PV = make_idesc_bf16(128, D, 0, 1);
+
+  extern __shared__ unsigned char dsm_raw[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages, M = a.M;
+  unsigned char* sQ = base + (size_t)S * 2 * TILE;
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(sQ + NPANEL * QPANEL);  // [S] tile landed
+  uint64_t* bar_empty = bar_full + S;                                      // [S] tile's MMAs retired
+  uint64_t* bar_s = bar_empty + S;                                         // [2] S buffer computed
+  uint64_t* bar_o = bar_s + 2;                                             // PV retired (one phase per tile)
+  uint64_t* bar_fin = bar_o + 1;                                           // all MMAs retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never = abort_flag + 1;  // stays 0: waits on it end by time only
+
+  const int s = blockIdx.x, bhk = blockIdx.y, b = bhk / a.Hkv, hk = bhk % a.Hkv;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nw = (int)(blockDim.x >> 5) - 1;  // softmax warps; warp nw is the producer
+  const int nsm = 32 * nw;
+  const int len = a.kv_lens ? min(max(__ldg(a.kv_lens + b), 0), a.Tkv) : a.Tkv;
+  const int kv0 = s * a.chunk, kv1 = min(kv0 + a.chunk, len);
+  const int ntiles = kv1 > kv0 ? (kv1 - kv0 + kDecKT - 1) / kDecKT : 0;
+  const int qbase = len - a.Tq;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(bar_full + i, 1);
+      mbar_init(bar_empty + i, 1);
+    }
+    mbar_init(bar_s, 1);
+    mbar_init(bar_s + 1, 1);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_fin, 1);
+    *abort_flag = 0;
+    *never = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  // Q operand: row m < M is query token (g, i) = (m / Tq, m % Tq) of head hk * G + g, other
+  // rows zero; 128-byte swizzled 64-column panels (the TMA layout of the K tiles).
+  for (int e = tid; e < 128 * (D / 8); e += blockDim.x) {
+    const int r = e / (D / 8), c = e % (D / 8);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (r < M) {
+      const uint16_t* qh = reinterpret_cast<const uint16_t*>(a.q.ptr) + (int64_t)b * a.q.stride_b +
+                           (int64_t)(hk * a.G + r / a.Tq) * a.q.stride_h + (int64_t)(r % a.Tq) * a.q.stride_t +
+                           c * 8;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) w[u] = (uint32_t)qh[2 * u] | ((uint32_t)qh[2 * u + 1] << 16);
+    }
+    *reinterpret_cast<uint4*>(sQ + (c >> 3) * QPANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == nw) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t % S;
+        if (t >= S && !mbar_wait(bar_empty + st, (uint32_t)(((t / S) - 1) & 1), abort_flag)) break;
+        unsigned char* dst = base + (size_t)st * 2 * TILE;
+        mbar_arrive_expect_tx(bar_full + st, 2 * TILE);
+#pragma unroll
+        for (int p = 0; p < NPANEL; ++p) {
+          tma_load_4d(dst + p * kPanelBytes, &tk, bar_full + st, p * 64, kv0 + t * kDecKT, hk, b);
+          tma_load_4d(dst + TILE + p * kPanelBytes, &tv, bar_full + st, p * 64, kv0 + t * kDecKT, hk, b);
+        }
+        issued = t + 1;
+      }
+      if (*abort_flag) report_status(a.status, FA_ERR_TIMEOUT);
+      // every stage's latest load lands before the CTA may exit (earlier uses were consumed)
+      for (int t = max(0, issued - S); t < issued; ++t)
+        mbar_wait(bar_full + t % S, (uint32_t)((t / S) & 1), never);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax + MMA issue
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+    const int r = tid;
+    const bool real = r < M;
+    const int qpos = qbase + r % a.Tq;
+    const float slope =
+        (real && (a.score.flags & FA_SCORE_ALIBI)) ? a.score.alibi_slopes[hk * a.G + r / a.Tq] : 0.f;
+    const bool softcap = (a.score.flags & FA_SCORE_SOFTCAP) != 0;
+    const bool plain = !softcap && !(a.score.flags & FA_SCORE_ALIBI);
+    const float cap = softcap ? a.score.softcap : 1.f, inv_cap = 1.f / cap;
+    int lo = 0, hi = real ? len - 1 : -1;  // allowed cache positions of this row
+    if (a.mask.flags & FA_MASK_CAUSAL) hi = min(hi, qpos);
+    if (a.mask.flags & FA_MASK_WINDOW) {
+      if (a.mask.window_left >= 0) lo = max(lo, qpos - a.mask.window_left);
+      if (a.mask.window_right >= 0) hi = min(hi, qpos + a.mask.window_right);
+    }
+    const float k_log2 = a.scale * kLog2e;
+    const uint32_t q_lo = (uint32_t)make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B);
+    const uint32_t desc_hi = (uint32_t)(make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B) >> 32);
+    const uint32_t k_lo0 = (uint32_t)make_smem_desc(smem_u32(base), 16, 1024, SMEM_SWIZZLE_128B);
+    const uint32_t v_lo0 = (uint32_t)make_smem_desc(smem_u32(base), kPanelBytes, 1024, SMEM_SWIZZLE_128B);
+
+    // warp 0: S(t) into buffer t & 1 once tile t has landed; false on timeout
+    auto issue_s = [&](int t) -> bool {
+      const int st = t % S;
+      if (!mbar_wait_w(bar_full + st, (uint32_t)((t / S) & 1), abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t k_lo = k_lo0 + (uint32_t)((st * 2 * TILE) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        mma_ss_w(tmem + TM_S + (t & 1) * kDecKT, q_lo + (kk >> 2) * (QPANEL >> 4) + (kk & 3) * 2, desc_hi,
+                 k_lo + (kk >> 2) * (kPanelBytes >> 4) + (kk & 3) * 2, desc_hi, IDESC_S, kk > 0);
+      tc_commit_w(bar_s + (t & 1));
+      return true;
+    };
+    if (warp == 0) {
+      bool ok = true;
+      for (int t = 0; t < min(2, ntiles) && ok; ++t) ok = issue_s(t);
+      if (!ok && lane == 0) *abort_flag = 1;
+    }
+
+    float m_use = -INFINITY, l_run = 0.f;
+    for (int it = 0; it < ntiles; ++it) {
+      const int st = it % S, t0 = kv0 + it * kDecKT, n = min(kDecKT, kv1 - t0);
+      const uint32_t tS = t_lane + TM_S + (it & 1) * kDecKT;
+      const bool got = mbar_wait(bar_s + (it & 1), (uint32_t)((it >> 1) & 1), abort_flag);
+      if (bar_red_or(1, nsm, !got)) {
+        if (tid == 0) *abort_flag = 1;  // the producer stops waiting for stages too
+        break;
+      }
+      tc_fence_after();
+      float x[kDecKT];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS, r0);
+        tmem_ld32(tS + 32, r1);
+        tmem_ld_wait();
+        reg_pin(r0);
+        reg_pin(r1);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          x[c] = __uint_as_float(r0[c]);
+          x[32 + c] = __uint_as_float(r1[c]);
+        }
+      }
+      // log2-domain logits; rows whose every key of the tile is allowed (and padding rows,
+      // whose values are never used) skip the mask when the whole warp can
+      const bool inside = !real || (lo <= t0 && t0 + kDecKT - 1 <= hi);
+      if (plain && __all_sync(0xffffffffu, inside)) {
+#pragma unroll
+        for (int c = 0; c < kDecKT; c += 2) {
+          const float2 y = __fmul2_rn(make_float2(x[c], x[c + 1]), make_float2(k_log2, k_log2));
+          x[c] = y.x;
+          x[c + 1] = y.y;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kDecKT; ++c) {
+          const int kv = t0 + c;
+          float sc = fmaf(slope, (float)(kv - qpos), x[c] * a.scale);
+          if (softcap) sc = cap * fast_tanh(sc * inv_cap);
+          x[c] = (kv >= lo && kv <= hi) ? sc * kLog2e : -INFINITY;
+        }
+      }
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = fmax3f(x[k], x[8 + k], x[16 + k]);
+#pragma unroll
+      for (int c = 24; c < kDecKT; c += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], c + 8 + k < kDecKT ? x[c + 8 + k] : -INFINITY);
+      const float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_use + kDecRescaleThreshold) {  // also the first finite max (m_use = -inf)
+        if (m_use != -INFINITY) {               // O holds earlier tiles' sums at the old reference
+          alpha = ex2_approx(m_use - mx);
+          rescale = true;
+        }
+        m_use = mx;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // PV(it - 1) must have retired before O is touched
+        if (it > 0 && !mbar_wait(bar_o, (uint32_t)((it - 1) & 1), abort_flag)) {
+          if (lane == 0) *abort_flag = 1;
+        } else {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t ov[32];
+            tmem_ld32(t_lane + TM_O + c0, ov);
+            tmem_ld_wait();
+            reg_pin(ov);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+            tmem_st32(t_lane + TM_O + c0, ov);
+          }
+        }
+      }
+      l_run *= alpha;
+      const float mref = m_use == -INFINITY ? 0.f : m_use;
+      uint32_t pk[kDecKT / 2];
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int c = 0; c < kDecKT; c += 2) {
+        const float2 y = __fadd2_rn(make_float2(x[c], x[c + 1]), make_float2(-mref, -mref));
+        const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+        sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
+        pk[c >> 1] = pack_bf16x2(p.x, p.y);
+      }
+      const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+      const float2 s4 = __fadd2_rn(s01, s23);
+      l_run += s4.x + s4.y;
+      tmem_st32(tS, pk);
+      if (n < kDecKT) {  // tile rows past the chunk's end hold other data: zero them in V
+        unsigned char* vst = base + (size_t)st * 2 * TILE + TILE;
+        for (int e = tid; e < (kDecKT - n) * (D / 8); e += nsm)
+          *reinterpret_cast<uint4*>(vst + chunk_off(n + e / (D / 8), e % (D / 8))) = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      bar_sync_n(1, nsm);
+      if (warp == 0) {
+        tc_fence_after();
+        const uint32_t v_lo = v_lo0 + (uint32_t)((st * 2 * TILE + TILE) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kDecKT / 16; ++kk)
+          mma_ts_w(tmem + TM_O, tmem + TM_S + (it & 1) * kDecKT + kk * 8, v_lo + kk * (2048 >> 4), desc_hi,
+                   IDESC_PV, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit_w(bar_empty + st);
+        tc_commit_w(bar_o);
+        if (it + 2 < ntiles && !*abort_flag && !issue_s(it + 2) && lane == 0) *abort_flag = 1;
+      }
+    }
+    // ---- wait for the last MMAs (also after an abort), then the epilogue
+    if (warp == 0) tc_commit_w(bar_fin);
+    const bool fin = mbar_wait(bar_fin, 0, never);
+    const bool good = fin && !*abort_flag;
+    if (!good && tid == 0) report_status(a.status, FA_ERR_TIMEOUT);
+    tc_fence_after();
+    const int64_t rows = (int64_t)a.B * a.H * a.Tq;
+    const int64_t row = ((int64_t)b * a.H + hk * a.G + r / a.Tq) * a.Tq + r % a.Tq;
+    const bool have_o = good && ntiles > 0;
+    const bool live = have_o && l_run > 0.f;
+    const float inv = live ? 1.f / l_run : 0.f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t ov[32];
+      if (have_o) {
+        tmem_ld32(t_lane + TM_O + c0, ov);
+        tmem_ld_wait();
+        reg_pin(ov);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) ov[c] = 0u;
+      }
+      if (real && good) {
+        float4* dst = reinterpret_cast<float4*>(a.part_o + ((int64_t)s * rows + row) * D + c0);
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          dst[v] = make_float4(__uint_as_float(ov[4 * v]) * inv, __uint_as_float(ov[4 * v + 1]) * inv,
+                               __uint_as_float(ov[4 * v + 2]) * inv, __uint_as_float(ov[4 * v + 3]) * inv);
+      }
+    }
+    if (real && good) a.part_lse[(int64_t)s * rows + row] = live ? (m_use + __log2f(l_run)) * kLn2 : -INFINITY;
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+// One warp per output row: log-sum-exp merge of the chunks' partials into o and lse.  The
+// lanes first stride over the chunks for the max and the weights exp(lse_s - max) (kept in
+// shared memory), then over the head dimension, summing the weighted partials chunk by chunk.
+constexpr int kMaxSplits = 256;
+
+template <typename T, int D>
 __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeArgs a) {
+  __shared__ float w_sh[8][kMaxSplits];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
   if (row >= rows) return;
+  float* w = w_sh[warp];
   float L = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) L = fmaxf(L, a.part_lse[(int64_t)s * rows + row]);
+  for (int s = lane; s < a.splits; s += 32) L = fmaxf(L, a.part_lse[(int64_t)s * rows + row]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) L = fmaxf(L, __shfl_xor_sync(0xffffffffu, L, o));
   float wsum = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
+  for (int s = lane; s < a.splits; s += 32) {
     const float ls = a.part_lse[(int64_t)s * rows + row];
-    wsum += ls == -INFINITY ? 0.f : expf(ls - L);
+    const float ws = ls == -INFINITY ? 0.f : expf(ls - L);
+    w[s] = ws;
+    wsum += ws;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+  __syncwarp();
+  float acc[D / 32];
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) acc[j] = 0.f;
+  const float* po = a.part_o + row * D + lane;
+#pragma unroll 4
+  for (int s = 0; s < a.splits; ++s) {
+    const float ws = w[s];
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) acc[j] = fmaf(ws, po[(int64_t)s * rows * D + 32 * j], acc[j]);
   }
   const int i = (int)(row % a.Tq), bh = (int)(row / a.Tq), b = bh / a.H, h = bh % a.H;
   T* o = reinterpret_cast<T*>(a.o.ptr) + (int64_t)b * a.o.stride_b + (int64_t)h * a.o.stride_h +
          (int64_t)i * a.o.stride_t;
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  for (int d = lane; d < a.D; d += 32) {
-    float acc = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ls = a.part_lse[(int64_t)s * rows + row];
-      if (ls != -INFINITY) acc = fmaf(expf(ls - L), a.part_o[((int64_t)s * rows + row) * a.D + d], acc);
-    }
-    if constexpr (sizeof(T) == 4) o[d] = acc * inv;
-    else o[d] = __float2bfloat16_rn(acc * inv);
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    if constexpr (sizeof(T) == 4) o[lane + 32 * j] = acc[j] * inv;
+    else o[lane + 32 * j] = __float2bfloat16_rn(acc[j] * inv);
   }
   if (lane == 0) a.lse[row] = wsum > 0.f ? L + logf(wsum) : -INFINITY;
 }
 
 // Chunking and pipeline depth for a call.
 struct DecodePlan {
-  int splits, chunk, stages;
+  int splits, chunk, stages, threads;
+  bool tc;  // tcgen05 kernel (bf16) or the CUDA-core kernel (fp32)
   size_t smem;
 };
 
@@ -355,25 +751,66 @@ DecodePlan plan_decode(const FaDecodeParams* p) {
   const int es = p->dtype == FA_DTYPE_F32 ? 4 : 2;
   const int M = (p->H / p->H_kv) * p->Tq;
   int sp = p->num_splits;
-  if (sp <= 0) {  // about four CTAs per SM across the grid, chunks of at least 256 cache rows
-    const int ctas = p->B * p->H_kv;
-    sp = (4 * 148 + ctas - 1) / ctas;
-    const int max_sp = (p->Tkv + 255) / 256;
-    if (sp > max_sp) sp = max_sp;
-    if (sp < 1) sp = 1;
+  if (sp <= 0) {
+    // Chunks of at least 256 cache rows.  The tcgen05 kernel runs one CTA per SM: take the
+    // smallest chunk count whose grid fills its last wave of 148 CTAs to >= 85 % (the most
+    // filled one if none does, up to four waves).  The CUDA-core kernel: about four CTAs per SM.
+    const int pairs = p->B * p->H_kv;
+    const int max_sp = std::max(1, std::min(kMaxSplits, (p->Tkv + 255) / 256));
+    if (p->dtype == FA_DTYPE_BF16) {
+      int best = 1;
+      double best_eff = -1.0;
+      for (int c = 1; c <= max_sp; ++c) {
+        const double waves = (double)pairs * c / 148.0;
+        if (waves > 4.0 && c > 1) break;
+        const double eff = waves / std::ceil(waves);
+        if (eff > best_eff + 1e-9) {
+          best_eff = eff;
+          best = c;
+        }
+        if (eff >= 0.85) break;
+      }
+      sp = best;
+    } else {
+      sp = std::min(max_sp, std::max(1, (4 * 148 + pairs - 1) / pairs));
+    }
   }
+  if (sp > kMaxSplits) sp = kMaxSplits;
   if (sp > p->Tkv) sp = p->Tkv;
   int ch = (p->Tkv + sp - 1) / sp;
   ch = (ch + kDecKT - 1) / kDecKT * kDecKT;  // chunks start on tile boundaries
   pl.chunk = ch;
   pl.splits = (p->Tkv + ch - 1) / ch;
-  // stages: as many (<= 4) as leave room for two CTAs per SM; else two, else one
+  if (p->dtype == FA_DTYPE_BF16) {
+    // tcgen05 kernel: as many CTAs per SM as TMEM holds (512 columns / the CTA's allocation),
+    // 2..4 stages in that share of the 228 KB of shared memory, and never less shared memory
+    // than keeps one more CTA out (an SM must not host more CTAs than TMEM serves at once).
+    // One CTA per SM with as many stages (<= 8) as its shared memory holds: a tile's load
+    // takes microseconds under load, so several must be in flight per SM.  The request never
+    // falls below what keeps a second CTA out (TMEM holds 512 columns per SM).
+    const size_t sm_total = 233472, reserved = 1024, max_dyn = 232448;
+    const size_t fixed = decode_tc_smem_bytes(p->D, 0), stage = decode_tc_smem_bytes(p->D, 1) - fixed;
+    int S = (int)((max_dyn - fixed) / stage);
+    S = std::max(2, std::min(8, S));
+    size_t smem = decode_tc_smem_bytes(p->D, S);
+    const size_t floor_bytes = sm_total / 2 - reserved + 1;
+    if (smem < floor_bytes) smem = floor_bytes;
+    pl.stages = S;
+    pl.smem = smem;
+    pl.threads = 32 * ((M + 31) / 32) + 32;  // softmax warps + the producer warp
+    pl.tc = true;
+    return pl;
+  }
+  // CUDA-core kernel (fp32): as many stages (<= 4) as leave room for two CTAs per SM; else
+  // two, else one
   const size_t fixed = decode_smem_bytes(p->D, es, M, 0), stage = decode_smem_bytes(p->D, es, M, 1) - fixed;
   const size_t two_ctas = 113 * 1024, one_cta = 220 * 1024;
   int S = fixed + stage <= two_ctas ? (int)((two_ctas - fixed) / stage) : (fixed + 2 * stage <= one_cta ? 2 : 1);
   if (S > 4) S = 4;
   pl.stages = S;
   pl.smem = decode_smem_bytes(p->D, es, M, S);
+  pl.threads = kDecThreads;
+  pl.tc = false;
   return pl;
 }
 
@@ -392,9 +829,10 @@ int check_decode(const FaDecodeParams* p) {
     snprintf(msg, sizeof(msg), "fa_decode: head dim %d (supported: 64, 128, 256)", p->D);
     return set_last_error(FA_ERR_UNSUPPORTED, msg);
   }
-  if ((p->H / p->H_kv) * p->Tq > kDecMaxRows) {
-    snprintf(msg, sizeof(msg), "fa_decode: H / H_kv * Tq = %d query rows per K/V head (at most %d)",
-             (p->H / p->H_kv) * p->Tq, kDecMaxRows);
+  const int max_rows = p->dtype == FA_DTYPE_BF16 ? kDecMaxRowsTc : kDecMaxRows;
+  if ((int64_t)(p->H / p->H_kv) * p->Tq > max_rows) {
+    snprintf(msg, sizeof(msg), "fa_decode: H / H_kv * Tq = %lld query rows per K/V head (at most %d for this dtype)",
+             (long long)(p->H / p->H_kv) * p->Tq, max_rows);
     return set_last_error(FA_ERR_UNSUPPORTED, msg);
   }
   if (p->Tq > p->Tkv) return set_last_error(FA_ERR_INVALID, "fa_decode: Tq > Tkv");
@@ -424,15 +862,35 @@ cudaError_t launch_split(const CUtensorMap& tk, const CUtensorMap& tv, const Dec
   return cudaGetLastError();
 }
 
+template <int D>
+cudaError_t launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a, const DecodePlan& pl,
+                      cudaStream_t stream) {
+  cudaError_t e =
+      cudaFuncSetAttribute(decode_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  if (e != cudaSuccess) return e;
+  decode_tc_kernel<D><<<dim3((unsigned)a.splits, (unsigned)(a.B * a.Hkv)), pl.threads, pl.smem, stream>>>(tk, tv, a);
+  return cudaGetLastError();
+}
+
 template <typename T>
-cudaError_t launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a, size_t smem,
+cudaError_t launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a, const DecodePlan& pl,
                           cudaStream_t stream) {
-  cudaError_t e = a.D == 64    ? launch_split<T, 64>(tk, tv, a, smem, stream)
-                  : a.D == 128 ? launch_split<T, 128>(tk, tv, a, smem, stream)
-                               : launch_split<T, 256>(tk, tv, a, smem, stream);
+  cudaError_t e;
+  if constexpr (sizeof(T) == 2) {
+    e = a.D == 64    ? launch_tc<64>(tk, tv, a, pl, stream)
+        : a.D == 128 ? launch_tc<128>(tk, tv, a, pl, stream)
+                     : launch_tc<256>(tk, tv, a, pl, stream);
+  } else {
+    e = a.D == 64    ? launch_split<T, 64>(tk, tv, a, pl.smem, stream)
+        : a.D == 128 ? launch_split<T, 128>(tk, tv, a, pl.smem, stream)
+                     : launch_split<T, 256>(tk, tv, a, pl.smem, stream);
+  }
   if (e != cudaSuccess) return e;
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
-  decode_merge_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(a);
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (a.D == 64) decode_merge_kernel<T, 64><<<blocks, 256, 0, stream>>>(a);
+  else if (a.D == 128) decode_merge_kernel<T, 128><<<blocks, 256, 0, stream>>>(a);
+  else decode_merge_kernel<T, 256><<<blocks, 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -493,9 +951,8 @@ int fa_decode(const FaDecodeParams* p, void* workspace, size_t workspace_bytes, 
   a.part_o = reinterpret_cast<float*>(workspace);
   a.part_lse = a.part_o + (size_t)pl.splits * rows * p->D;
   a.status = p->status;
-  cudaError_t e = p->dtype == FA_DTYPE_F32
-                      ? fa::launch_decode<float>(tk, tv, a, pl.smem, (cudaStream_t)stream)
-                      : fa::launch_decode<__nv_bfloat16>(tk, tv, a, pl.smem, (cudaStream_t)stream);
+  cudaError_t e = p->dtype == FA_DTYPE_F32 ? fa::launch_decode<float>(tk, tv, a, pl, (cudaStream_t)stream)
+                                           : fa::launch_decode<__nv_bfloat16>(tk, tv, a, pl, (cudaStream_t)stream);
   if (e != cudaSuccess) {
     snprintf(msg, sizeof(msg), "fa_decode: %s", cudaGetErrorString(e));
     return fa::set_last_error(FA_ERR_CUDA, msg);

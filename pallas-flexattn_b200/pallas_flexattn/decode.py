@@ -10,7 +10,8 @@ before it.
 
 The cache is cut into chunks handled by separate CTAs (one per chunk, batch and K/V head,
 covering every query head of the group); a second kernel merges the chunks by
-log-sum-exp.  There is no CPU path.
+log-sum-exp.  bf16 runs on the tensor cores (tcgen05), fp32 on CUDA cores.  There is no
+CPU path.
 """
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ from .mask_mod import spec_of as mask_spec_of
 from .score_mod import ScoreMod
 from .score_mod import spec_of as score_spec_of
 
-MAX_QUERY_ROWS = 64  # (H / H_kv) * Tq per K/V head
+MAX_QUERY_ROWS = {"bf16": 128, "fp32": 64}  # (H / H_kv) * Tq per K/V head
 
 
 def flash_attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

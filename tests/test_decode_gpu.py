@@ -2,8 +2,8 @@
 the CPU oracle's decode_reference, at the bf16 / fp32 tolerance of the attention tests
 (|err| <= atol + 2^-8 |ref| element-wise and relative-L2 <= rtol; lse within 2e-3).
 
-Cases cover single-token and multi-token decode, grouped-query heads up to the 64-row
-limit, head dims 64 / 128 / 256, ragged per-sequence cache lengths (not multiples of the
+Cases cover single-token and multi-token decode, grouped-query heads up to the row limits
+(128 for bf16 on the tcgen05 kernel, 64 for fp32 on the CUDA-core kernel), head dims 64 / 128 / 256, ragged per-sequence cache lengths (not multiples of the
 64-row tile, down to Tq), chunkings with empty chunks, causal and sliding-window masks,
 ALiBi and softcap (bf16 only: the softcap's tanh is the hardware approximation, about
 2^-11 relative), fp32 inputs, and a cache stored as [B, T, H_kv, D] (strided heads).
@@ -41,6 +41,9 @@ CASES = {
     "gqa4_t4_window_alibi_d64": (2, 16, 4, 4, 777, 64, torch.bfloat16, [777, 130], "window", "alibi", 0),
     "mqa_t2_softcap_d256_splits5": (2, 4, 1, 2, 900, 256, torch.bfloat16, [2, 899], "causal", "softcap", 5),
     "rows64_d128": (1, 16, 1, 4, 1536, 128, torch.bfloat16, [1500], "causal", "both", 0),
+    "rows128_d64": (2, 32, 1, 4, 1000, 64, torch.bfloat16, [1000, 260], "causal", None, 0),
+    "rows96_d256_window": (1, 24, 1, 4, 700, 256, torch.bfloat16, [699], "window", None, 0),
+    "fp32_rows64": (1, 32, 2, 4, 300, 64, torch.float32, [300], "causal", None, 0),
     "many_splits_empty_chunks": (2, 2, 2, 1, 4096, 64, torch.bfloat16, [65, 4096], None, None, 40),
     "no_lens_d64": (2, 8, 2, 3, 640, 64, torch.bfloat16, None, "causal", None, 0),
     "fp32_d64": (2, 4, 2, 2, 500, 64, torch.float32, [500, 77], "causal", "alibi", 0),
@@ -53,10 +56,10 @@ def _mods(kind, H):
     if kind is None:
         return None, ()
     if kind == "alibi":
-        return pf.alibi_score_mod(pf.alibi_slopes(H)), (O.alibi(O.alibi_slopes(H)),)
+        return pf.alibi_score_mod(H), (O.alibi(O.alibi_slopes(H)),)
     if kind == "softcap":
         return pf.softcap_score_mod(15.0), (O.softcap(15.0),)
-    return (pf.compose_score_mods(pf.alibi_score_mod(pf.alibi_slopes(H)), pf.softcap_score_mod(15.0)),
+    return (pf.compose_score_mods(pf.alibi_score_mod(H), pf.softcap_score_mod(15.0)),
             (O.alibi(O.alibi_slopes(H)), O.softcap(15.0)))
 
 
@@ -121,9 +124,12 @@ def test_decode_rejects_unsupported_requests():
     q, k, v = _inputs(1, 4, 4, 1, 128, 96, torch.bfloat16, seed=0)
     with pytest.raises(L.FlexAttnError):
         pf.flash_attention_decode(q, k, v)  # head dim 96
-    q, k, v = _inputs(1, 64, 1, 2, 128, 64, torch.bfloat16, seed=0)
+    q, k, v = _inputs(1, 64, 1, 3, 128, 64, torch.bfloat16, seed=0)
     with pytest.raises(L.FlexAttnError):
-        pf.flash_attention_decode(q, k, v)  # 128 query rows per K/V head
+        pf.flash_attention_decode(q, k, v)  # 192 query rows per K/V head
+    q, k, v = _inputs(1, 32, 1, 3, 128, 64, torch.float32, seed=0)
+    with pytest.raises(L.FlexAttnError):
+        pf.flash_attention_decode(q, k, v)  # 96 query rows: fp32 allows 64
     q, k, v = _inputs(1, 4, 4, 1, 128, 64, torch.bfloat16, seed=0)
     with pytest.raises(NotImplementedError):
         pf.flash_attention_decode(q, k, v, None, pf.document_mask([64, 64]))

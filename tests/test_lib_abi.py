@@ -65,7 +65,7 @@ def test_decode_validation_without_gpu():
     assert lib.fa_decode_workspace_size(C.byref(dp), C.byref(size)) == 0
     assert size.value == 3 * rows * 129 * 4 + 256
     for field, value, code, text in [("D", 96, L.FA_ERR_UNSUPPORTED, b"head dim"),
-                                     ("Tq", 17, L.FA_ERR_UNSUPPORTED, b"query rows"),
+                                     ("Tq", 33, L.FA_ERR_UNSUPPORTED, b"query rows"),
                                      ("H_kv", 3, L.FA_ERR_INVALID, b"multiple"),
                                      ("Tkv", 0, L.FA_ERR_INVALID, b"shape")]:
         bad = L.FaDecodeParams.from_buffer_copy(dp)
