@@ -369,9 +369,9 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
 //   O += P V    (A = P from TMEM, B = V from shared memory, MN-major; N = D).
 // The padded rows cost tensor-core time only, of which decode has plenty: a tile's HBM bytes
 // take longer than its MMAs.  Warps: ceil(M / 32) softmax warps (those whose TMEM lanes hold
-// real rows; warp 0 also issues the MMAs) and one producer warp that streams K/V tiles
-// through the stage ring, refilling a stage as soon as the PV MMA that read it completes
-// (per-stage empty barriers committed by the MMA issuer).  The row max used for P moves only
+// real rows), one MMA-issue warp and one producer warp that streams K/V tiles through the
+// stage ring, refilling a stage as soon as the PV MMA that read it completes (per-stage
+// empty barriers committed by the MMA issuer).  The row max used for P moves only
 // when a tile's max exceeds it by more than 8 (log2 units): O is rescaled rarely and P <= 256.
 constexpr float kDecRescaleThreshold = 8.f;
 
@@ -381,6 +381,12 @@ __host__ __device__ constexpr uint32_t decode_tc_tmem_cols(int D) { return D <= 
 inline size_t decode_tc_smem_bytes(int D, int stages) {
   return 1024 + (size_t)stages * 2 * kDecKT * D * 2 + (size_t)128 * D * 2 + 256;
 }
+
+// CTAs per SM of the tcgen05 kernel.  Head dim 64: two (5 stages each), as a 16 KB tile
+// gives one softmax chain too little time per byte (measured 5.0 vs 2.7 TB/s on
+// B32 H16 Tkv8192).  Head dim 128: one CTA with 6 stages measured 3 % faster than two with
+// 2; head dim 256: one (its fixed part and two stages fill the SM).
+inline int decode_tc_ctas_per_sm(int D) { return D <= 64 ? 2 : 1; }
 
 __device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
   uint32_t r;
@@ -399,7 +405,7 @@ __device__ __forceinline__ void bar_sync_n(int id, int nthreads) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ CUtensorMap tk,
+__global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ CUtensorMap tk,
                                                         const __grid_constant__ CUtensorMap tv, const DecodeArgs a) {
   constexpr int TILE = kDecKT * D * 2;  // bytes of a 64-row K or V tile
   constexpr int QPANEL = 128 * 128;     // bytes of one 64-column panel of the 128-row Q operand
@@ -413,11 +419,15 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages, M = a.M;
+  const int nw = (int)(blockDim.x >> 5) - 2;  // softmax warps; then the MMA warp and the producer warp
+  const int nsm = 32 * nw;
+  const int mma_warp = nw, prod_warp = nw + 1;
   unsigned char* sQ = base + (size_t)S * 2 * TILE;
   uint64_t* bar_full = reinterpret_cast<uint64_t*>(sQ + NPANEL * QPANEL);  // [S] tile landed
   uint64_t* bar_empty = bar_full + S;                                      // [S] tile's MMAs retired
   uint64_t* bar_s = bar_empty + S;                                         // [2] S buffer computed
-  uint64_t* bar_o = bar_s + 2;                                             // PV retired (one phase per tile)
+  uint64_t* bar_p = bar_s + 2;                                             // [2] P buffer written (nw arrivals)
+  uint64_t* bar_o = bar_p + 2;                                             // PV retired (one phase per tile)
   uint64_t* bar_fin = bar_o + 1;                                           // all MMAs retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -425,8 +435,6 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
 
   const int s = blockIdx.x, bhk = blockIdx.y, b = bhk / a.Hkv, hk = bhk % a.Hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nw = (int)(blockDim.x >> 5) - 1;  // softmax warps; warp nw is the producer
-  const int nsm = 32 * nw;
   const int len = a.kv_lens ? min(max(__ldg(a.kv_lens + b), 0), a.Tkv) : a.Tkv;
   const int kv0 = s * a.chunk, kv1 = min(kv0 + a.chunk, len);
   const int ntiles = kv1 > kv0 ? (kv1 - kv0 + kDecKT - 1) / kDecKT : 0;
@@ -437,8 +445,10 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       mbar_init(bar_full + i, 1);
       mbar_init(bar_empty + i, 1);
     }
-    mbar_init(bar_s, 1);
-    mbar_init(bar_s + 1, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_s + i, 1);
+      mbar_init(bar_p + i, nw);
+    }
     mbar_init(bar_o, 1);
     mbar_init(bar_fin, 1);
     *abort_flag = 0;
@@ -470,7 +480,7 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == nw) {
+  if (warp == prod_warp) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tk);
@@ -488,14 +498,53 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
         }
         issued = t + 1;
       }
-      if (*abort_flag) report_status(a.status, FA_ERR_TIMEOUT);
       // every stage's latest load lands before the CTA may exit (earlier uses were consumed)
       for (int t = max(0, issued - S); t < issued; ++t)
         mbar_wait(bar_full + t % S, (uint32_t)((t / S) & 1), never);
     }
     __syncwarp();
+  } else if (warp == mma_warp) {
+    // ------------------------------------------------------------------ MMA issue
+    // Order: S(0), S(1), then per tile PV(t) once its P is written, and S(t + 2) into the
+    // buffer PV(t) has just read (the tensor pipe runs one issuer's MMAs in order).
+    const uint32_t q_lo = (uint32_t)make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B);
+    const uint32_t desc_hi = (uint32_t)(make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B) >> 32);
+    const uint32_t k_lo0 = (uint32_t)make_smem_desc(smem_u32(base), 16, 1024, SMEM_SWIZZLE_128B);
+    const uint32_t v_lo0 = (uint32_t)make_smem_desc(smem_u32(base), kPanelBytes, 1024, SMEM_SWIZZLE_128B);
+    auto issue_s = [&](int t) -> bool {
+      const int st = t % S;
+      if (!mbar_wait_w(bar_full + st, (uint32_t)((t / S) & 1), abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t k_lo = k_lo0 + (uint32_t)((st * 2 * TILE) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        mma_ss_w(tmem + TM_S + (t & 1) * kDecKT, q_lo + (kk >> 2) * (QPANEL >> 4) + (kk & 3) * 2, desc_hi,
+                 k_lo + (kk >> 2) * (kPanelBytes >> 4) + (kk & 3) * 2, desc_hi, IDESC_S, kk > 0);
+      tc_commit_w(bar_s + (t & 1));
+      return true;
+    };
+    bool ok = true;
+    for (int t = 0; t < min(2, ntiles) && ok; ++t) ok = issue_s(t);
+    for (int it = 0; it < ntiles && ok; ++it) {
+      const int st = it % S;
+      if (!mbar_wait_w(bar_p + (it & 1), (uint32_t)((it >> 1) & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t v_lo = v_lo0 + (uint32_t)((st * 2 * TILE + TILE) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < kDecKT / 16; ++kk)
+        mma_ts_w(tmem + TM_O, tmem + TM_S + (it & 1) * kDecKT + kk * 8, v_lo + kk * (2048 >> 4), desc_hi,
+                 IDESC_PV, (it > 0 || kk > 0) ? 1u : 0u);
+      tc_commit_w(bar_empty + st);
+      tc_commit_w(bar_o);
+      if (it + 2 < ntiles) ok = issue_s(it + 2);
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+    tc_commit_w(bar_fin);
   } else {
-    // ------------------------------------------------------------------ softmax + MMA issue
+    // ------------------------------------------------------------------ softmax (thread = row)
     const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
     const int r = tid;
     const bool real = r < M;
@@ -512,29 +561,6 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       if (a.mask.window_right >= 0) hi = min(hi, qpos + a.mask.window_right);
     }
     const float k_log2 = a.scale * kLog2e;
-    const uint32_t q_lo = (uint32_t)make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B);
-    const uint32_t desc_hi = (uint32_t)(make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B) >> 32);
-    const uint32_t k_lo0 = (uint32_t)make_smem_desc(smem_u32(base), 16, 1024, SMEM_SWIZZLE_128B);
-    const uint32_t v_lo0 = (uint32_t)make_smem_desc(smem_u32(base), kPanelBytes, 1024, SMEM_SWIZZLE_128B);
-
-    // warp 0: S(t) into buffer t & 1 once tile t has landed; false on timeout
-    auto issue_s = [&](int t) -> bool {
-      const int st = t % S;
-      if (!mbar_wait_w(bar_full + st, (uint32_t)((t / S) & 1), abort_flag)) return false;
-      tc_fence_after();
-      const uint32_t k_lo = k_lo0 + (uint32_t)((st * 2 * TILE) >> 4);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        mma_ss_w(tmem + TM_S + (t & 1) * kDecKT, q_lo + (kk >> 2) * (QPANEL >> 4) + (kk & 3) * 2, desc_hi,
-                 k_lo + (kk >> 2) * (kPanelBytes >> 4) + (kk & 3) * 2, desc_hi, IDESC_S, kk > 0);
-      tc_commit_w(bar_s + (t & 1));
-      return true;
-    };
-    if (warp == 0) {
-      bool ok = true;
-      for (int t = 0; t < min(2, ntiles) && ok; ++t) ok = issue_s(t);
-      if (!ok && lane == 0) *abort_flag = 1;
-    }
 
     float m_use = -INFINITY, l_run = 0.f;
     for (int it = 0; it < ntiles; ++it) {
@@ -542,7 +568,7 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       const uint32_t tS = t_lane + TM_S + (it & 1) * kDecKT;
       const bool got = mbar_wait(bar_s + (it & 1), (uint32_t)((it >> 1) & 1), abort_flag);
       if (bar_red_or(1, nsm, !got)) {
-        if (tid == 0) *abort_flag = 1;  // the producer stops waiting for stages too
+        if (tid == 0) *abort_flag = 1;  // the MMA and producer warps stop waiting too
         break;
       }
       tc_fence_after();
@@ -560,17 +586,13 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
           x[32 + c] = __uint_as_float(r1[c]);
         }
       }
-      // log2-domain logits; rows whose every key of the tile is allowed (and padding rows,
-      // whose values are never used) skip the mask when the whole warp can
+      // Rows whose every key of the tile is allowed (and padding rows, whose values are
+      // never used) keep raw logits when the whole warp can: the max is taken on them and
+      // the scale folds into the exponent's FMA.  Otherwise x becomes the masked
+      // log2-domain logit.
       const bool inside = !real || (lo <= t0 && t0 + kDecKT - 1 <= hi);
-      if (plain && __all_sync(0xffffffffu, inside)) {
-#pragma unroll
-        for (int c = 0; c < kDecKT; c += 2) {
-          const float2 y = __fmul2_rn(make_float2(x[c], x[c + 1]), make_float2(k_log2, k_log2));
-          x[c] = y.x;
-          x[c + 1] = y.y;
-        }
-      } else {
+      const bool fast = plain && __all_sync(0xffffffffu, inside);
+      if (!fast) {
 #pragma unroll
         for (int c = 0; c < kDecKT; ++c) {
           const int kv = t0 + c;
@@ -586,7 +608,8 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       for (int c = 24; c < kDecKT; c += 16)
 #pragma unroll
         for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], c + 8 + k < kDecKT ? x[c + 8 + k] : -INFINITY);
-      const float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      if (fast) mx *= k_log2;  // k_log2 > 0
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_use + kDecRescaleThreshold) {  // also the first finite max (m_use = -inf)
@@ -616,11 +639,13 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       }
       l_run *= alpha;
       const float mref = m_use == -INFINITY ? 0.f : m_use;
+      const float kk = fast ? k_log2 : 1.f;
+      const float2 k2 = make_float2(kk, kk), nm2 = make_float2(-mref, -mref);
       uint32_t pk[kDecKT / 2];
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c = 0; c < kDecKT; c += 2) {
-        const float2 y = __fadd2_rn(make_float2(x[c], x[c + 1]), make_float2(-mref, -mref));
+        const float2 y = __ffma2_rn(make_float2(x[c], x[c + 1]), k2, nm2);
         const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
         sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
         pk[c >> 1] = pack_bf16x2(p.x, p.y);
@@ -637,21 +662,10 @@ __global__ void __launch_bounds__(160) decode_tc_kernel(const __grid_constant__ 
       }
       tmem_st_wait();
       tc_fence_before();
-      bar_sync_n(1, nsm);
-      if (warp == 0) {
-        tc_fence_after();
-        const uint32_t v_lo = v_lo0 + (uint32_t)((st * 2 * TILE + TILE) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < kDecKT / 16; ++kk)
-          mma_ts_w(tmem + TM_O, tmem + TM_S + (it & 1) * kDecKT + kk * 8, v_lo + kk * (2048 >> 4), desc_hi,
-                   IDESC_PV, (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_w(bar_empty + st);
-        tc_commit_w(bar_o);
-        if (it + 2 < ntiles && !*abort_flag && !issue_s(it + 2) && lane == 0) *abort_flag = 1;
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p + (it & 1));
     }
     // ---- wait for the last MMAs (also after an abort), then the epilogue
-    if (warp == 0) tc_commit_w(bar_fin);
     const bool fin = mbar_wait(bar_fin, 0, never);
     const bool good = fin && !*abort_flag;
     if (!good && tid == 0) report_status(a.status, FA_ERR_TIMEOUT);
@@ -752,16 +766,17 @@ DecodePlan plan_decode(const FaDecodeParams* p) {
   const int M = (p->H / p->H_kv) * p->Tq;
   int sp = p->num_splits;
   if (sp <= 0) {
-    // Chunks of at least 256 cache rows.  The tcgen05 kernel runs one CTA per SM: take the
-    // smallest chunk count whose grid fills its last wave of 148 CTAs to >= 85 % (the most
-    // filled one if none does, up to four waves).  The CUDA-core kernel: about four CTAs per SM.
+    // Chunks of at least 256 cache rows.  The tcgen05 kernel: take the smallest chunk count
+    // whose grid fills its last wave (148 SMs x CTAs per SM) to >= 85 % (the most filled one
+    // if none does, up to four waves).  The CUDA-core kernel: about four CTAs per SM.
     const int pairs = p->B * p->H_kv;
     const int max_sp = std::max(1, std::min(kMaxSplits, (p->Tkv + 255) / 256));
     if (p->dtype == FA_DTYPE_BF16) {
+      const double slots = 148.0 * decode_tc_ctas_per_sm(p->D);
       int best = 1;
       double best_eff = -1.0;
       for (int c = 1; c <= max_sp; ++c) {
-        const double waves = (double)pairs * c / 148.0;
+        const double waves = (double)pairs * c / slots;
         if (waves > 4.0 && c > 1) break;
         const double eff = waves / std::ceil(waves);
         if (eff > best_eff + 1e-9) {
@@ -785,19 +800,21 @@ DecodePlan plan_decode(const FaDecodeParams* p) {
     // tcgen05 kernel: as many CTAs per SM as TMEM holds (512 columns / the CTA's allocation),
     // 2..4 stages in that share of the 228 KB of shared memory, and never less shared memory
     // than keeps one more CTA out (an SM must not host more CTAs than TMEM serves at once).
-    // One CTA per SM with as many stages (<= 8) as its shared memory holds: a tile's load
-    // takes microseconds under load, so several must be in flight per SM.  The request never
-    // falls below what keeps a second CTA out (TMEM holds 512 columns per SM).
+    // Stages: as many (2..8) as the CTA's share of the SM's 228 KB of shared memory holds; a
+    // tile's load takes microseconds under load, so several must be in flight per SM.  The
+    // request never falls below what keeps one more CTA out (TMEM holds 512 columns per SM).
+    const int per_sm = decode_tc_ctas_per_sm(p->D);
     const size_t sm_total = 233472, reserved = 1024, max_dyn = 232448;
+    const size_t budget = std::min(max_dyn, sm_total / per_sm - reserved);
     const size_t fixed = decode_tc_smem_bytes(p->D, 0), stage = decode_tc_smem_bytes(p->D, 1) - fixed;
-    int S = (int)((max_dyn - fixed) / stage);
+    int S = (int)((budget - fixed) / stage);
     S = std::max(2, std::min(8, S));
     size_t smem = decode_tc_smem_bytes(p->D, S);
-    const size_t floor_bytes = sm_total / 2 - reserved + 1;
+    const size_t floor_bytes = sm_total / (per_sm + 1) - reserved + 1;
     if (smem < floor_bytes) smem = floor_bytes;
     pl.stages = S;
     pl.smem = smem;
-    pl.threads = 32 * ((M + 31) / 32) + 32;  // softmax warps + the producer warp
+    pl.threads = 32 * ((M + 31) / 32) + 64;  // softmax warps, the MMA warp, the producer warp
     pl.tc = true;
     return pl;
   }
