@@ -21,6 +21,10 @@ the timed region) and ``gpu_launches``.
 ``--impl reference`` times the reference's CPU implementation of the path (the
 restatement in oracle/cpu_reference.py; the reference itself needs jax, which
 is not installed) on this box's host cores, on rank 0 only.
+
+``--workload decode [--decode-config gqa_b64]`` prints a separate line for the
+split-KV decode path (K/V cache bytes read per second against the measured HBM
+bandwidth); the default workload is the forward+backward step above.
 """
 from __future__ import annotations
 
@@ -329,8 +333,17 @@ def main():
     ap.add_argument("--impl", default="flexattn", choices=["flexattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="train", choices=["train", "decode"],
+                    help="train: forward+backward step (the headline); decode: split-KV decode")
+    ap.add_argument("--decode-config", default="gqa_b64", choices=sorted(DECODE_CONFIGS))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "decode":
+        dist, rank, world, local = dist_setup()
+        rc = run_decode(args, dist, rank, world, local)
+        if dist is not None:
+            dist.destroy_process_group()
+        return rc
 
     from pallas_flexattn import workloads as W
 
@@ -501,6 +514,139 @@ def main():
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+    return 0
+
+
+DECODE_CONFIGS = {
+    # name: (B, H, H_kv, Tq, Tkv, D) -- grouped-query decode of one new token per sequence
+    "gqa_b64": (64, 32, 8, 1, 4096, 128),  # Llama-3-8B-like heads, 4k context, batch 64
+    "gqa_b8": (8, 32, 8, 1, 8192, 128),    # smaller case (ncu captures)
+    "mha_b32_d64": (32, 16, 16, 1, 8192, 64),
+}
+
+
+def run_decode(args, dist, rank, world, local) -> int:
+    """Split-KV decode (flash_attention_decode) against a resident bf16 K/V cache: the
+    metric is cache bytes read per second (K and V, every valid row once per call), the
+    roofline the measured HBM copy bandwidth.  One step = one call for all B sequences."""
+    import numpy as np
+
+    import pallas_flexattn as pf
+    from pallas_flexattn import flash_attn as FA
+
+    B, H, Hkv, Tq, Tkv, D = DECODE_CONFIGS[args.decode_config]
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "workload": f"decode_{args.decode_config}",
+                              "unavailable": "the reference has no decode (K/V cache) path"}), flush=True)
+        return 0
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    g = torch.Generator(device="cpu").manual_seed(2000 + rank)
+    kc, vc = (torch.randn(B, Hkv, Tkv, D, generator=g).to(device, torch.bfloat16) for _ in range(2))
+    q = torch.randn(B, H, Tq, D, generator=g).to(device, torch.bfloat16)
+    lens = torch.full((B,), Tkv, dtype=torch.int32, device=device)
+    cache_bytes = 2 * B * Hkv * Tkv * D * 2
+
+    def step():
+        return pf.flash_attention_decode(q, kc, vc, lens, pf.causal_mask)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    FA.check_device_status(device)
+
+    def timed(fn, n):
+        barrier(dist)
+        torch.cuda.synchronize()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(n):
+            fn()
+        e_ev.record()
+        torch.cuda.synchronize()
+        barrier(dist)
+        return s_ev.elapsed_time(e_ev) / n
+
+    with ClockSampler(device) as clk:
+        ms = max_over_ranks(dist, timed(step, args.steps), device)
+    FA.check_device_status(device)
+    value = cache_bytes * world / (ms * 1e-3) / 1e9
+    peak = float(peaks["hbm_gbs"])
+
+    e2e = None
+    if not args.no_e2e:
+        # A serving step: the new tokens' q and their K/V rows come from pinned host memory
+        # (appended to the cache on the device), the output rows go back to the host.
+        hq = q.detach().cpu().pin_memory()
+        hk, hv = (torch.randn(B, Hkv, Tq, D).to(torch.bfloat16).pin_memory() for _ in range(2))
+        dq = torch.empty_like(q)
+        out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            kc[:, :, Tkv - Tq:].copy_(hk, non_blocking=True)
+            vc[:, :, Tkv - Tq:].copy_(hv, non_blocking=True)
+            o, _ = pf.flash_attention_decode(dq, kc, vc, lens, pf.causal_mask)
+            out_host.copy_(o, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        ms_e2e = max_over_ranks(dist, timed(e2e_step, args.steps), device)
+        e2e = {"value": cache_bytes * world / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
+               "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
+
+    # parity: two sequences of the timed inputs against the oracle
+    parity = None
+    if rank == 0:
+        from oracle import flexattn_oracle as O
+
+        o, lse = step()
+        torch.cuda.synchronize()
+        sl = slice(0, 2)
+        qn, kn, vn = (t[sl].float().cpu().numpy().astype(np.float64) for t in (q, kc, vc))
+        ro, rl = O.decode_reference(qn, kn, vn, [Tkv] * 2, O.causal)
+        got = o[sl].float().cpu().numpy()
+        diff = np.abs(got - ro)
+        rel = float(np.linalg.norm(got - ro) / max(np.linalg.norm(ro), 1e-30))
+        ok = bool((diff - (2e-2 + 2.0 ** -8 * np.abs(ro))).max() <= 0 and rel <= 5e-3)
+        parity = {"o": {"max_abs": round(float(diff.max()), 6), "rel_l2": round(rel, 7)},
+                  "lse_max_abs": round(float(np.abs(lse[sl].cpu().numpy() - rl).max()), 6),
+                  "slice": "b = 0, 1 of the timed inputs", "pass": ok}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import flexattn_oracle as O
+
+        qn, kn, vn = (t[:1].float().cpu().numpy().astype(np.float64) for t in (q, kc, vc))
+        reps, t_tot = 0, 0.0
+        while t_tot < 8.0 and reps < 200:
+            t0 = time.perf_counter()
+            O.decode_reference(qn, kn, vn, [Tkv], O.causal)
+            t_tot += time.perf_counter() - t0
+            reps += 1
+        per = t_tot / reps
+        cpu = {"value": cache_bytes / B / per / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{reps} x oracle decode_reference of one sequence (numpy fp64, Tkv={Tkv}); "
+                         f"{per * 1e3:.1f} ms per sequence"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode K/V cache read GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": f"decode_{args.decode_config}", "B": B, "H": H, "H_kv": Hkv, "Tq": Tq,
+                       "Tkv": Tkv, "D": D, "mask": "causal",
+                       "l2": f"cache {cache_bytes / 1e6:.0f} MB per rank, larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel + decode_merge_kernel (one fa_decode call)",
+                         "achieved": value / world, "peak": peak, "unit": "GB/s", "frac": value / world / peak,
+                         "peak_source": f"hbm_gbs ({peaks['source']})", "traffic": None},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
+            "parity": parity,
+        }
+        print(json.dumps(line), flush=True)
     return 0
 
 
