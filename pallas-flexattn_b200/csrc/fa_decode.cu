@@ -375,18 +375,40 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
 // when a tile's max exceeds it by more than 8 (log2 units): O is rescaled rarely and P <= 256.
 constexpr float kDecRescaleThreshold = 8.f;
 
-__host__ __device__ constexpr uint32_t decode_tc_tmem_cols(int D) { return D <= 128 ? 256u : 512u; }
+// Cache rows per tile of the tcgen05 kernel (the S MMA's N and the TMA box height).  A
+// 128-row tile halves the per-tile fixed costs of the softmax warp (waits, TMEM round
+// trips, barrier arrivals) at head dim 128; head dims 64 and 256 keep 64 rows (64: two CTAs
+// per SM fit only with 64-row tiles; 256: shared memory holds two 64-row stages).
+#ifndef FA_DEC_KT_D64
+#define FA_DEC_KT_D64 64
+#endif
+#ifndef FA_DEC_KT_D128
+#define FA_DEC_KT_D128 128
+#endif
+__host__ __device__ constexpr int decode_tc_kt(int D) {
+  return D <= 64 ? FA_DEC_KT_D64 : (D <= 128 ? FA_DEC_KT_D128 : 64);
+}
+
+// TMEM columns: two S buffers of KT fp32 columns and O (D columns), rounded to a power of 2.
+__host__ __device__ constexpr uint32_t decode_tc_tmem_cols(int D, int KT) { return 2 * KT + D <= 256 ? 256u : 512u; }
 
 // Dynamic shared memory of the tcgen05 kernel: K/V stages, the 128-row Q operand, barriers.
 inline size_t decode_tc_smem_bytes(int D, int stages) {
-  return 1024 + (size_t)stages * 2 * kDecKT * D * 2 + (size_t)128 * D * 2 + 256;
+  return 1024 + (size_t)stages * 2 * decode_tc_kt(D) * D * 2 + (size_t)128 * D * 2 + 256;
 }
 
-// CTAs per SM of the tcgen05 kernel.  Head dim 64: two (5 stages each), as a 16 KB tile
-// gives one softmax chain too little time per byte (measured 5.0 vs 2.7 TB/s on
-// B32 H16 Tkv8192).  Head dim 128: one CTA with 6 stages measured 3 % faster than two with
-// 2; head dim 256: one (its fixed part and two stages fill the SM).
-inline int decode_tc_ctas_per_sm(int D) { return D <= 64 ? 2 : 1; }
+// Byte offset of 16-byte chunk c of row r in a tile of 128-byte swizzled panels of PANEL
+// bytes each (panel c / 8, chunk slot (c % 8) ^ (r % 8) of the row's 128-byte line).
+template <int PANEL>
+__device__ __forceinline__ uint32_t chunk_off_p(int r, int c) {
+  return (uint32_t)((c >> 3) * PANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// CTAs per SM of the tcgen05 kernel: as many as TMEM serves (512 columns), at most two.
+// Head dim 64 with 64-row tiles: two (5 stages each), as a 16 KB tile gives one softmax
+// chain too little time per byte (measured 5.0 vs 2.7 TB/s on B32 H16 Tkv8192).  Head dim
+// 128 (128-row tiles) and 256: one.
+inline int decode_tc_ctas_per_sm(int D) { return decode_tc_tmem_cols(D, decode_tc_kt(D)) <= 256 ? 2 : 1; }
 
 __device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
   uint32_t r;
@@ -400,19 +422,17 @@ __device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
       : "memory");
   return r != 0;
 }
-__device__ __forceinline__ void bar_sync_n(int id, int nthreads) {
-  asm volatile("barrier.cta.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
 
-template <int D>
+template <int D, int KT>
 __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ CUtensorMap tk,
                                                         const __grid_constant__ CUtensorMap tv, const DecodeArgs a) {
-  constexpr int TILE = kDecKT * D * 2;  // bytes of a 64-row K or V tile
+  constexpr int TILE = KT * D * 2;  // bytes of a KT-row K or V tile
+  constexpr int PANELB = KT * 128;  // bytes of one 64-column panel of a tile
   constexpr int QPANEL = 128 * 128;     // bytes of one 64-column panel of the 128-row Q operand
   constexpr int NPANEL = D / 64;
-  constexpr uint32_t TM_COLS = decode_tc_tmem_cols(D);
-  constexpr uint32_t TM_S = 0, TM_O = 2 * kDecKT;  // S buffers at 0 and 64 (fp32; P over them as bf16), O
-  constexpr uint32_t IDESC_S = make_idesc_bf16(128, kDecKT, 0, 0);
+  constexpr uint32_t TM_COLS = decode_tc_tmem_cols(D, KT);
+  constexpr uint32_t TM_S = 0, TM_O = 2 * KT;  // S buffers at 0 and KT (fp32; P over them as bf16), O
+  constexpr uint32_t IDESC_S = make_idesc_bf16(128, KT, 0, 0);
   constexpr uint32_t IDESC_PV = make_idesc_bf16(128, D, 0, 1);
 
   extern __shared__ unsigned char dsm_raw[];
@@ -437,7 +457,7 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int len = a.kv_lens ? min(max(__ldg(a.kv_lens + b), 0), a.Tkv) : a.Tkv;
   const int kv0 = s * a.chunk, kv1 = min(kv0 + a.chunk, len);
-  const int ntiles = kv1 > kv0 ? (kv1 - kv0 + kDecKT - 1) / kDecKT : 0;
+  const int ntiles = kv1 > kv0 ? (kv1 - kv0 + KT - 1) / KT : 0;
   const int qbase = len - a.Tq;
 
   if (tid == 0) {
@@ -493,8 +513,8 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
         mbar_arrive_expect_tx(bar_full + st, 2 * TILE);
 #pragma unroll
         for (int p = 0; p < NPANEL; ++p) {
-          tma_load_4d(dst + p * kPanelBytes, &tk, bar_full + st, p * 64, kv0 + t * kDecKT, hk, b);
-          tma_load_4d(dst + TILE + p * kPanelBytes, &tv, bar_full + st, p * 64, kv0 + t * kDecKT, hk, b);
+          tma_load_4d(dst + p * PANELB, &tk, bar_full + st, p * 64, kv0 + t * KT, hk, b);
+          tma_load_4d(dst + TILE + p * PANELB, &tv, bar_full + st, p * 64, kv0 + t * KT, hk, b);
         }
         issued = t + 1;
       }
@@ -510,7 +530,7 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
     const uint32_t q_lo = (uint32_t)make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B);
     const uint32_t desc_hi = (uint32_t)(make_smem_desc(smem_u32(sQ), 16, 1024, SMEM_SWIZZLE_128B) >> 32);
     const uint32_t k_lo0 = (uint32_t)make_smem_desc(smem_u32(base), 16, 1024, SMEM_SWIZZLE_128B);
-    const uint32_t v_lo0 = (uint32_t)make_smem_desc(smem_u32(base), kPanelBytes, 1024, SMEM_SWIZZLE_128B);
+    const uint32_t v_lo0 = (uint32_t)make_smem_desc(smem_u32(base), PANELB, 1024, SMEM_SWIZZLE_128B);
     auto issue_s = [&](int t) -> bool {
       const int st = t % S;
       if (!mbar_wait_w(bar_full + st, (uint32_t)((t / S) & 1), abort_flag)) return false;
@@ -518,8 +538,8 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
       const uint32_t k_lo = k_lo0 + (uint32_t)((st * 2 * TILE) >> 4);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
-        mma_ss_w(tmem + TM_S + (t & 1) * kDecKT, q_lo + (kk >> 2) * (QPANEL >> 4) + (kk & 3) * 2, desc_hi,
-                 k_lo + (kk >> 2) * (kPanelBytes >> 4) + (kk & 3) * 2, desc_hi, IDESC_S, kk > 0);
+        mma_ss_w(tmem + TM_S + (t & 1) * KT, q_lo + (kk >> 2) * (QPANEL >> 4) + (kk & 3) * 2, desc_hi,
+                 k_lo + (kk >> 2) * (PANELB >> 4) + (kk & 3) * 2, desc_hi, IDESC_S, kk > 0);
       tc_commit_w(bar_s + (t & 1));
       return true;
     };
@@ -534,8 +554,8 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
       tc_fence_after();
       const uint32_t v_lo = v_lo0 + (uint32_t)((st * 2 * TILE + TILE) >> 4);
 #pragma unroll
-      for (int kk = 0; kk < kDecKT / 16; ++kk)
-        mma_ts_w(tmem + TM_O, tmem + TM_S + (it & 1) * kDecKT + kk * 8, v_lo + kk * (2048 >> 4), desc_hi,
+      for (int kk = 0; kk < KT / 16; ++kk)
+        mma_ts_w(tmem + TM_O, tmem + TM_S + (it & 1) * KT + kk * 8, v_lo + kk * (2048 >> 4), desc_hi,
                  IDESC_PV, (it > 0 || kk > 0) ? 1u : 0u);
       tc_commit_w(bar_empty + st);
       tc_commit_w(bar_o);
@@ -564,37 +584,36 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
 
     float m_use = -INFINITY, l_run = 0.f;
     for (int it = 0; it < ntiles; ++it) {
-      const int st = it % S, t0 = kv0 + it * kDecKT, n = min(kDecKT, kv1 - t0);
-      const uint32_t tS = t_lane + TM_S + (it & 1) * kDecKT;
+      const int st = it % S, t0 = kv0 + it * KT, n = min(KT, kv1 - t0);
+      const uint32_t tS = t_lane + TM_S + (it & 1) * KT;
       const bool got = mbar_wait(bar_s + (it & 1), (uint32_t)((it >> 1) & 1), abort_flag);
       if (bar_red_or(1, nsm, !got)) {
         if (tid == 0) *abort_flag = 1;  // the MMA and producer warps stop waiting too
         break;
       }
       tc_fence_after();
-      float x[kDecKT];
+      float x[KT];
       {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tS, r0);
-        tmem_ld32(tS + 32, r1);
-        tmem_ld_wait();
-        reg_pin(r0);
-        reg_pin(r1);
+        uint32_t rr[KT / 32][32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          x[c] = __uint_as_float(r0[c]);
-          x[32 + c] = __uint_as_float(r1[c]);
+        for (int h = 0; h < KT / 32; ++h) tmem_ld32(tS + 32 * h, rr[h]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < KT / 32; ++h) {
+          reg_pin(rr[h]);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) x[32 * h + c] = __uint_as_float(rr[h][c]);
         }
       }
       // Rows whose every key of the tile is allowed (and padding rows, whose values are
       // never used) keep raw logits when the whole warp can: the max is taken on them and
       // the scale folds into the exponent's FMA.  Otherwise x becomes the masked
       // log2-domain logit.
-      const bool inside = !real || (lo <= t0 && t0 + kDecKT - 1 <= hi);
+      const bool inside = !real || (lo <= t0 && t0 + KT - 1 <= hi);
       const bool fast = plain && __all_sync(0xffffffffu, inside);
       if (!fast) {
 #pragma unroll
-        for (int c = 0; c < kDecKT; ++c) {
+        for (int c = 0; c < KT; ++c) {
           const int kv = t0 + c;
           float sc = fmaf(slope, (float)(kv - qpos), x[c] * a.scale);
           if (softcap) sc = cap * fast_tanh(sc * inv_cap);
@@ -605,9 +624,9 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
 #pragma unroll
       for (int k = 0; k < 8; ++k) m8[k] = fmax3f(x[k], x[8 + k], x[16 + k]);
 #pragma unroll
-      for (int c = 24; c < kDecKT; c += 16)
+      for (int c = 24; c < KT; c += 16)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], c + 8 + k < kDecKT ? x[c + 8 + k] : -INFINITY);
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], c + 8 + k < KT ? x[c + 8 + k] : -INFINITY);
       float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       if (fast) mx *= k_log2;  // k_log2 > 0
       float alpha = 1.f;
@@ -641,23 +660,26 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
       const float mref = m_use == -INFINITY ? 0.f : m_use;
       const float kk = fast ? k_log2 : 1.f;
       const float2 k2 = make_float2(kk, kk), nm2 = make_float2(-mref, -mref);
-      uint32_t pk[kDecKT / 2];
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < kDecKT; c += 2) {
-        const float2 y = __ffma2_rn(make_float2(x[c], x[c + 1]), k2, nm2);
-        const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-        sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
-        pk[c >> 1] = pack_bf16x2(p.x, p.y);
+      for (int h = 0; h < KT / 64; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float2 y = __ffma2_rn(make_float2(x[64 * h + c], x[64 * h + c + 1]), k2, nm2);
+          const float2 p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+          sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
+          pk[c >> 1] = pack_bf16x2(p.x, p.y);
+        }
+        tmem_st32(tS + 32 * h, pk);
       }
       const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
       const float2 s4 = __fadd2_rn(s01, s23);
       l_run += s4.x + s4.y;
-      tmem_st32(tS, pk);
-      if (n < kDecKT) {  // tile rows past the chunk's end hold other data: zero them in V
+      if (n < KT) {  // tile rows past the chunk's end hold other data: zero them in V
         unsigned char* vst = base + (size_t)st * 2 * TILE + TILE;
-        for (int e = tid; e < (kDecKT - n) * (D / 8); e += nsm)
-          *reinterpret_cast<uint4*>(vst + chunk_off(n + e / (D / 8), e % (D / 8))) = make_uint4(0, 0, 0, 0);
+        for (int e = tid; e < (KT - n) * (D / 8); e += nsm)
+          *reinterpret_cast<uint4*>(vst + chunk_off_p<PANELB>(n + e / (D / 8), e % (D / 8))) = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
       }
       tmem_st_wait();
@@ -792,8 +814,9 @@ DecodePlan plan_decode(const FaDecodeParams* p) {
   }
   if (sp > kMaxSplits) sp = kMaxSplits;
   if (sp > p->Tkv) sp = p->Tkv;
+  const int kt = p->dtype == FA_DTYPE_BF16 ? decode_tc_kt(p->D) : kDecKT;
   int ch = (p->Tkv + sp - 1) / sp;
-  ch = (ch + kDecKT - 1) / kDecKT * kDecKT;  // chunks start on tile boundaries
+  ch = (ch + kt - 1) / kt * kt;  // chunks start on tile boundaries
   pl.chunk = ch;
   pl.splits = (p->Tkv + ch - 1) / ch;
   if (p->dtype == FA_DTYPE_BF16) {
@@ -882,10 +905,12 @@ cudaError_t launch_split(const CUtensorMap& tk, const CUtensorMap& tv, const Dec
 template <int D>
 cudaError_t launch_tc(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a, const DecodePlan& pl,
                       cudaStream_t stream) {
+  constexpr int KT = decode_tc_kt(D);
   cudaError_t e =
-      cudaFuncSetAttribute(decode_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+      cudaFuncSetAttribute(decode_tc_kernel<D, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
-  decode_tc_kernel<D><<<dim3((unsigned)a.splits, (unsigned)(a.B * a.Hkv)), pl.threads, pl.smem, stream>>>(tk, tv, a);
+  decode_tc_kernel<D, KT>
+      <<<dim3((unsigned)a.splits, (unsigned)(a.B * a.Hkv)), pl.threads, pl.smem, stream>>>(tk, tv, a);
   return cudaGetLastError();
 }
 
@@ -942,8 +967,9 @@ int fa_decode(const FaDecodeParams* p, void* workspace, size_t workspace_bytes, 
     return fa::set_last_error(FA_ERR_INVALID, msg);
   }
   CUtensorMap tk, tv;
-  if ((rc = fa::make_row_tile_map(&tk, p->k, p->dtype, p->B, p->H_kv, p->Tkv, p->D, fa::kDecKT, "k")) ||
-      (rc = fa::make_row_tile_map(&tv, p->v, p->dtype, p->B, p->H_kv, p->Tkv, p->D, fa::kDecKT, "v")))
+  const int box_rows = pl.tc ? fa::decode_tc_kt(p->D) : fa::kDecKT;
+  if ((rc = fa::make_row_tile_map(&tk, p->k, p->dtype, p->B, p->H_kv, p->Tkv, p->D, box_rows, "k")) ||
+      (rc = fa::make_row_tile_map(&tv, p->v, p->dtype, p->B, p->H_kv, p->Tkv, p->D, box_rows, "v")))
     return rc;
   fa::DecodeArgs a;
   a.B = p->B;
