@@ -361,8 +361,8 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
 
 // ---------------------------------------------------------------------------------------------
 // tcgen05 split kernel (bf16).  The query rows of the group (M <= 128, zero-padded to 128) are
-// the MMA's M dimension and the 64-row cache tile its N:
-//   S = Q K^T   (kind::f16, M = 128, N = 64, K = D; Q and K from shared memory) into one of two
+// the MMA's M dimension and the KT-row cache tile its N:
+//   S = Q K^T   (kind::f16, M = 128, N = KT, K = D; Q and K from shared memory) into one of two
 //               TMEM score buffers, so the next tile's S is computed during this tile's softmax,
 //   P = exp2(S - m) by the warps that own the rows (thread = row, as in the forward kernel),
 //               written back over S in TMEM as bf16,
