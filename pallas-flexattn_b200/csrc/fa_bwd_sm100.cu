@@ -496,11 +496,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int hh = 0; hh < NP / 32; ++hh) {
         uint32_t s[32];
         tmem_ld32(t_lane + C::TM_S + cbase + 32 * hh, s);
+        // lse2 of the group's 32 q columns: one coalesced load (lane = column), then
+        // register shuffles; broadcast loads from shared memory would cost one
+        // shared-memory wavefront per 4 values on the pipe the MMAs' operand reads need.
         float l2[32];
+        {
+          const float lv = lse2[32 * hh + lane];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 v4 = reinterpret_cast<const float4*>(lse2 + 32 * hh)[u];
-          l2[4 * u] = v4.x; l2[4 * u + 1] = v4.y; l2[4 * u + 2] = v4.z; l2[4 * u + 3] = v4.w;
+          for (int c = 0; c < 32; ++c) l2[c] = __shfl_sync(0xffffffffu, lv, c);
         }
         tmem_ld_wait();
         reg_pin(s);
@@ -540,11 +543,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int hh = 0; hh < NP / 32; ++hh) {
         uint32_t dp[32];
         tmem_ld32(t_lane + C::TM_DP + cbase + 32 * hh, dp);
-        float dl32[32];
+        float dl32[32];  // delta of the group's columns, distributed as lse2 above
+        {
+          const float dv = dl[32 * hh + lane];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float4 v4 = reinterpret_cast<const float4*>(dl + 32 * hh)[u];
-          dl32[4 * u] = v4.x; dl32[4 * u + 1] = v4.y; dl32[4 * u + 2] = v4.z; dl32[4 * u + 3] = v4.w;
+          for (int c = 0; c < 32; ++c) dl32[c] = __shfl_sync(0xffffffffu, dv, c);
         }
         tmem_ld_wait();
         reg_pin(dp);
