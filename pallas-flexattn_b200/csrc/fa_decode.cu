@@ -43,6 +43,7 @@ constexpr int kPanelBytes = kDecKT * 128;
 
 struct DecodeArgs {
   int B, H, Hkv, Tq, Tkv, D, G, M, splits, chunk, stages;
+  int q_vec;  // q's base and strides are 16-byte multiples (the tcgen05 kernel loads 8 bf16 at once)
   FaTensor q, o;
   float* lse;
   const int32_t* kv_lens;
@@ -479,20 +480,46 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
     tmem_alloc(tmem_slot, TM_COLS);
     tmem_relinquish();
   }
+  __syncthreads();  // barriers initialised
+  // The producer starts the first tiles' loads before the Q operand is built, so a short
+  // chunk's first load overlaps the prologue.
+  int issued = 0;  // producer lane 0: tiles whose loads were issued
+  auto issue = [&](int t) {
+    const int st = t % S;
+    unsigned char* dst = base + (size_t)st * 2 * TILE;
+    mbar_arrive_expect_tx(bar_full + st, 2 * TILE);
+#pragma unroll
+    for (int p = 0; p < NPANEL; ++p) {
+      tma_load_4d(dst + p * PANELB, &tk, bar_full + st, p * 64, kv0 + t * KT, hk, b);
+      tma_load_4d(dst + TILE + p * PANELB, &tv, bar_full + st, p * 64, kv0 + t * KT, hk, b);
+    }
+    issued = t + 1;
+  };
+  if (warp == prod_warp && lane == 0) {
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+    for (int t = 0; t < min(S, ntiles); ++t) issue(t);
+  }
   // Q operand: row m < M is query token (g, i) = (m / Tq, m % Tq) of head hk * G + g, other
-  // rows zero; 128-byte swizzled 64-column panels (the TMA layout of the K tiles).
+  // rows zero; 128-byte swizzled 64-column panels (the TMA layout of the K tiles).  16-byte
+  // loads when q's base and strides allow them.
   for (int e = tid; e < 128 * (D / 8); e += blockDim.x) {
     const int r = e / (D / 8), c = e % (D / 8);
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
     if (r < M) {
       const uint16_t* qh = reinterpret_cast<const uint16_t*>(a.q.ptr) + (int64_t)b * a.q.stride_b +
                            (int64_t)(hk * a.G + r / a.Tq) * a.q.stride_h + (int64_t)(r % a.Tq) * a.q.stride_t +
                            c * 8;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) w[u] = (uint32_t)qh[2 * u] | ((uint32_t)qh[2 * u + 1] << 16);
+      if (a.q_vec) {
+        w = __ldg(reinterpret_cast<const uint4*>(qh));
+      } else {
+        w.x = (uint32_t)qh[0] | ((uint32_t)qh[1] << 16);
+        w.y = (uint32_t)qh[2] | ((uint32_t)qh[3] << 16);
+        w.z = (uint32_t)qh[4] | ((uint32_t)qh[5] << 16);
+        w.w = (uint32_t)qh[6] | ((uint32_t)qh[7] << 16);
+      }
     }
-    *reinterpret_cast<uint4*>(sQ + (c >> 3) * QPANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
-        make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(sQ + (c >> 3) * QPANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = w;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -503,20 +530,10 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
   if (warp == prod_warp) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      int issued = 0;
-      for (int t = 0; t < ntiles; ++t) {
+      for (int t = issued; t < ntiles; ++t) {
         const int st = t % S;
         if (t >= S && !mbar_wait(bar_empty + st, (uint32_t)(((t / S) - 1) & 1), abort_flag)) break;
-        unsigned char* dst = base + (size_t)st * 2 * TILE;
-        mbar_arrive_expect_tx(bar_full + st, 2 * TILE);
-#pragma unroll
-        for (int p = 0; p < NPANEL; ++p) {
-          tma_load_4d(dst + p * PANELB, &tk, bar_full + st, p * 64, kv0 + t * KT, hk, b);
-          tma_load_4d(dst + TILE + p * PANELB, &tv, bar_full + st, p * 64, kv0 + t * KT, hk, b);
-        }
-        issued = t + 1;
+        issue(t);
       }
       // every stage's latest load lands before the CTA may exit (earlier uses were consumed)
       for (int t = max(0, issued - S); t < issued; ++t)
@@ -984,6 +1001,8 @@ int fa_decode(const FaDecodeParams* p, void* workspace, size_t workspace_bytes, 
   a.chunk = pl.chunk;
   a.stages = pl.stages;
   a.q = p->q;
+  a.q_vec = (reinterpret_cast<uintptr_t>(p->q.ptr) % 16 == 0) && (p->q.stride_b * 2) % 16 == 0 &&
+            (p->q.stride_h * 2) % 16 == 0 && (p->q.stride_t * 2) % 16 == 0;
   a.o = p->o;
   a.lse = p->lse;
   a.kv_lens = p->kv_lens;
