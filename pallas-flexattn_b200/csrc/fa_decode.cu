@@ -44,6 +44,7 @@ constexpr int kPanelBytes = kDecKT * 128;
 struct DecodeArgs {
   int B, H, Hkv, Tq, Tkv, D, G, M, splits, chunk, stages;
   int q_vec;  // q's base and strides are 16-byte multiples (the tcgen05 kernel loads 8 bf16 at once)
+  int o_vec;  // the same for o (the tcgen05 kernel stores 8 bf16 at once when it writes o itself)
   FaTensor q, o;
   float* lse;
   const int32_t* kv_lens;
@@ -374,6 +375,8 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 2 : 1)
 // stage ring, refilling a stage as soon as the PV MMA that read it completes (per-stage
 // empty barriers committed by the MMA issuer).  The row max used for P moves only
 // when a tile's max exceeds it by more than 8 (log2 units): O is rescaled rarely and P <= 256.
+// With a single chunk (num_splits = 1) the CTA writes the final o and lse itself and no merge
+// kernel runs.
 constexpr float kDecRescaleThreshold = 8.f;
 
 // Cache rows per tile of the tcgen05 kernel (the S MMA's N and the TMA box height).  A
@@ -725,7 +728,25 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < 32; ++c) ov[c] = 0u;
       }
-      if (real && good) {
+      if (real && good && a.splits == 1) {  // one chunk: the final o, no merge
+        uint16_t* orow = reinterpret_cast<uint16_t*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
+                         (int64_t)(hk * a.G + r / a.Tq) * a.o.stride_h + (int64_t)(r % a.Tq) * a.o.stride_t + c0;
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2)
+          pk[c >> 1] = pack_bf16x2(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
+        if (a.o_vec) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            reinterpret_cast<uint4*>(orow)[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            orow[2 * c] = (uint16_t)(pk[c] & 0xffffu);
+            orow[2 * c + 1] = (uint16_t)(pk[c] >> 16);
+          }
+        }
+      } else if (real && good) {
         float4* dst = reinterpret_cast<float4*>(a.part_o + ((int64_t)s * rows + row) * D + c0);
 #pragma unroll
         for (int v = 0; v < 8; ++v)
@@ -733,7 +754,11 @@ __global__ void __launch_bounds__(192) decode_tc_kernel(const __grid_constant__ 
                                __uint_as_float(ov[4 * v + 2]) * inv, __uint_as_float(ov[4 * v + 3]) * inv);
       }
     }
-    if (real && good) a.part_lse[(int64_t)s * rows + row] = live ? (m_use + __log2f(l_run)) * kLn2 : -INFINITY;
+    if (real && good) {
+      const float lse = live ? (m_use + __log2f(l_run)) * kLn2 : -INFINITY;
+      if (a.splits == 1) a.lse[row] = lse;
+      else a.part_lse[(int64_t)s * rows + row] = lse;
+    }
     tc_fence_before();
   }
   __syncthreads();
@@ -945,6 +970,7 @@ cudaError_t launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const De
                      : launch_split<T, 256>(tk, tv, a, pl.smem, stream);
   }
   if (e != cudaSuccess) return e;
+  if (sizeof(T) == 2 && a.splits == 1) return cudaSuccess;  // the tcgen05 kernel wrote o and lse
   const int64_t rows = (int64_t)a.B * a.H * a.Tq;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   if (a.D == 64) decode_merge_kernel<T, 64><<<blocks, 256, 0, stream>>>(a);
@@ -1004,6 +1030,8 @@ int fa_decode(const FaDecodeParams* p, void* workspace, size_t workspace_bytes, 
   a.q_vec = (reinterpret_cast<uintptr_t>(p->q.ptr) % 16 == 0) && (p->q.stride_b * 2) % 16 == 0 &&
             (p->q.stride_h * 2) % 16 == 0 && (p->q.stride_t * 2) % 16 == 0;
   a.o = p->o;
+  a.o_vec = (reinterpret_cast<uintptr_t>(p->o.ptr) % 16 == 0) && (p->o.stride_b * 2) % 16 == 0 &&
+            (p->o.stride_h * 2) % 16 == 0 && (p->o.stride_t * 2) % 16 == 0;
   a.lse = p->lse;
   a.kv_lens = p->kv_lens;
   a.scale = p->scale;

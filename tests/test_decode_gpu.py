@@ -45,6 +45,8 @@ CASES = {
     "rows96_d256_window": (1, 24, 1, 4, 700, 256, torch.bfloat16, [699], "window", None, 0),
     "fp32_rows64": (1, 32, 2, 4, 300, 64, torch.float32, [300], "causal", None, 0),
     "many_splits_empty_chunks": (2, 2, 2, 1, 4096, 64, torch.bfloat16, [65, 4096], None, None, 40),
+    "one_chunk_writes_o_d128": (2, 16, 4, 2, 700, 128, torch.bfloat16, [700, 333], "causal", "alibi", 1),
+    "one_chunk_writes_o_d64": (3, 8, 8, 1, 300, 64, torch.bfloat16, [300, 1, 129], None, None, 1),
     "no_lens_d64": (2, 8, 2, 3, 640, 64, torch.bfloat16, None, "causal", None, 0),
     "fp32_d64": (2, 4, 2, 2, 500, 64, torch.float32, [500, 77], "causal", "alibi", 0),
     "fp32_d128": (1, 8, 1, 1, 700, 128, torch.float32, [650], None, "alibi", 0),
