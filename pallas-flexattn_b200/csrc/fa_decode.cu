@@ -3,21 +3,27 @@
 // Decode reads the whole cache once per call and does O(G * Tq) multiply-adds per cache
 // element, so with a handful of query rows it is bound by HBM bandwidth.  The cache of each
 // (b, K/V head) is cut into num_splits chunks; one CTA per (chunk, b, K/V head) handles
-// every query row of the K/V head's group (G = H / H_kv heads x Tq tokens = M rows,
-// M <= 64), so each cache element is read from HBM once for all of them.
+// every query row of the K/V head's group (G = H / H_kv heads x Tq tokens = M rows), so each
+// cache element is read from HBM once for all of them.  Query row i of batch b sits at
+// global position kv_lens[b] - Tq + i.  Two split kernels:
 //
-// Per CTA: TMA streams 64-row K and V tiles (128-byte swizzled panels) through a ring of
-// stages guarded by mbarriers; the 256 threads then run, per tile,
-//   scores   thread = (cache row j, every 4th query row): 16-byte K chunks against fp32 Q
-//            (the swizzle spreads the 32 rows a warp reads over all banks); with one or
-//            two query rows the threads split the head dimension instead,
-//   softmax  warp = query row, online (running max and sum per row),
-//   P V      thread = (8 output columns, every RG-th query row), fp32 accumulators in
-//            registers, probabilities read 4 cache rows at a time; with fewer query rows
-//            than RG the threads also split the tile's cache rows (partials added at the end),
-// and thread 0 refills the stage.  Each CTA writes its normalised partial (o, lse) to the
-// workspace; decode_merge_kernel combines the chunks by log-sum-exp.  Query row i of batch b
-// sits at global position kv_lens[b] - Tq + i.
+// * decode_tc_kernel (bf16, M <= 128): tcgen05 MMAs with the query rows as the MMA's M; its
+//   own comment below describes it.
+// * decode_split_kernel (fp32, M <= 64), on CUDA cores.  Per CTA, TMA streams 64-row K and V
+//   tiles (128-byte swizzled panels) through a ring of stages guarded by mbarriers; the 256
+//   threads then run, per tile,
+//     scores   thread = (cache row j, every 4th query row): 16-byte K chunks against fp32 Q
+//              (the swizzle spreads the 32 rows a warp reads over all banks); with one or
+//              two query rows the threads split the head dimension instead,
+//     softmax  warp = query row, online (running max and sum per row),
+//     P V      thread = (8 output columns, every RG-th query row), fp32 accumulators in
+//              registers, probabilities read 4 cache rows at a time; with fewer query rows
+//              than RG the threads also split the tile's cache rows (partials added at the end),
+//   and thread 0 refills the stage.
+//
+// Each CTA writes its normalised partial (o, lse) to the workspace and decode_merge_kernel
+// combines the chunks by log-sum-exp (the tcgen05 kernel writes o and lse itself when there
+// is a single chunk).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
