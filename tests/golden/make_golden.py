@@ -1,10 +1,10 @@
 """Generate golden vectors by running the reference's own source.
 
-    python tests/golden/make_golden.py [--reference-src PATH]
+    python tests/golden/make_golden.py --reference-src PATH
 
-Imports novastar53/pallas-flexattn from its source tree (default
-/root/reference/src, read-only) under the numpy stand-in for jax in
-jax_numpy_standin.py, and records:
+Imports novastar53/pallas-flexattn from its source tree (PATH is the project's ``src``
+directory, or the FLEXATTN_REFERENCE_SRC environment variable; it is only read) under the
+numpy stand-in for jax in jax_numpy_standin.py, and records:
 
 * block_masks.npz   create_block_mask (block_mask.py:54-129) on the reference's
                     mask_mods and on document / tile / band predicates, at the
@@ -20,6 +20,7 @@ Only this script reads the reference tree; the tests read the fixtures.
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -54,8 +55,11 @@ def block_mask_cases(ref_mm, np_doc, np_table):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--reference-src", default=os.environ.get("FLEXATTN_REFERENCE_SRC"),
+                    help="the reference project's src directory (read-only)")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("give --reference-src or set FLEXATTN_REFERENCE_SRC")
 
     sys.path.insert(0, str(HERE))
     import jax_numpy_standin
