@@ -189,8 +189,9 @@ FA_API int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes,
  * fail once the pool has reserved most of the HBM.
  * - Limit: a shape whose fa_bwd_workspace_size exceeds FA_NOALLOC_SCRATCH_BYTES returns
  *   FA_ERR_UNSUPPORTED before anything runs (use fa_bwd for it).
- * - The first call on each device, with that device current, resolves the scratch address
- *   and loads the kernels; make it before any stream capture.
+ * - The scratch's address belongs to a CUDA context: the first call in each context (a
+ *   device's primary context, or one the host created with cuCtxCreate), with that context
+ *   current, resolves it and loads the kernels; make that call before any stream capture.
  * - Calls that overlap on one device share the scratch and race: serialise them. */
 #define FA_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 FA_API int fa_bwd_noalloc(const FaBwdParams* p, fa_stream_t stream);

@@ -208,7 +208,10 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
   return FA_OK;
 }
 
-static int check_bwd(const FaBwdParams* p) {
+extern "C++" {
+namespace fa {
+// Argument validation shared by fa_bwd, fa_bwd_preprocess and fa_bwd_noalloc.
+int check_bwd_params(const FaBwdParams* p) {
   if (!p) return fail(FA_ERR_INVALID, "params is NULL");
   int rc = check_common(p->dtype, p->B, p->H, p->H_kv, p->Tq, p->Tkv, p->D, p->blocks, p->mask, p->score);
   if (rc) return rc;
@@ -224,6 +227,8 @@ static int check_bwd(const FaBwdParams* p) {
   if (p->blocks.q_cap <= 0) return fail(FA_ERR_INVALID, "q_cap must be positive");
   return FA_OK;
 }
+}  // namespace fa
+}  // extern "C++"
 
 static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -240,7 +245,7 @@ int fa_bwd_workspace_size(const FaBwdParams* p, size_t* bytes) {
 }
 
 int fa_bwd_preprocess(const FaBwdParams* p, float* delta, float* dq_accum, fa_stream_t stream) {
-  int rc = check_bwd(p);
+  int rc = check_bwd_params(p);
   if (rc) return rc;
   if (!delta || !dq_accum) return fail(FA_ERR_INVALID, "delta / dq_accum is NULL");
   AttnArgs a = base_args(p->B, p->H, p->H_kv, p->Tq, p->Tkv, p->D, p->scale, p->mask, p->score, p->blocks, p->status);
@@ -253,7 +258,7 @@ int fa_bwd_preprocess(const FaBwdParams* p, float* delta, float* dq_accum, fa_st
 }
 
 int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_stream_t stream) {
-  int rc = check_bwd(p);
+  int rc = check_bwd_params(p);
   if (rc) return rc;
   size_t need = 0;
   fa_bwd_workspace_size(p, &need);

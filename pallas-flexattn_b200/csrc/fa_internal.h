@@ -8,6 +8,8 @@
 namespace fa {
 
 int set_last_error(int code, const char* msg);
+// Validation of a backward call's parameters (the checks fa_bwd makes before any work).
+int check_bwd_params(const FaBwdParams* p);
 // 4-D tensor map over a [B, heads, T, D] tensor (bf16 or fp32): box = one 128-byte panel of
 // columns x box_rows rows, 128-byte swizzle.  Rejects misaligned bases and strides.
 int make_row_tile_map(CUtensorMap* map, const FaTensor& t, int dtype, int B, int heads, int T, int D, int box_rows,

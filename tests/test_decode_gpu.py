@@ -19,19 +19,14 @@ import pallas_flexattn as pf
 from oracle import flexattn_oracle as O
 from pallas_flexattn import _lib as L
 from pallas_flexattn.flash_attn import check_device_status
+from tolerance import assert_close
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
-TOL = {torch.bfloat16: (2e-2, 5e-3, 2.0 ** -8), torch.float32: (2e-4, 1e-5, 0.0)}
 
 
 def close(name, got, ref, dtype):
-    got = got.detach().float().cpu().numpy()
-    atol, rtol, elem_rel = TOL[dtype]
-    diff = np.abs(got - ref)
-    excess = float((diff - (atol + elem_rel * np.abs(ref))).max())
-    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), atol * math.sqrt(ref.size)))
-    assert excess <= 0 and rel <= rtol, f"{name}: max-abs {float(diff.max()):.3e}, rel-L2 {rel:.3e}"
+    assert_close(name, got.detach().float().cpu().numpy(), ref, bf16=dtype == torch.bfloat16)
 
 
 CASES = {

@@ -45,10 +45,16 @@ def test_error_path_without_gpu():
     bp.B, bp.H, bp.Tq, bp.D = 2, 3, 5, 64
     assert L.lib().fa_bwd_workspace_size(C.byref(bp), C.byref(size)) == 0
     assert size.value >= 2 * 3 * 5 * 4 + 2 * 3 * 5 * 64 * 4
-    # the no-alloc backward turns away a shape beyond its static scratch before any CUDA call
+    # the no-alloc backward validates like fa_bwd before it measures the shape against its
+    # static scratch, so a malformed call gets fa_bwd's error, not a scratch-size error
     bp.B, bp.H, bp.H_kv, bp.Tq, bp.Tkv, bp.D = 1, 16, 16, 8192, 8192, 128
-    assert L.lib().fa_bwd_noalloc(C.byref(bp), None) == L.FA_ERR_UNSUPPORTED
-    assert b"static scratch" in L.lib().fa_last_error()
+    assert L.lib().fa_bwd(C.byref(bp), None, 0, None) == L.FA_ERR_INVALID
+    msg = L.lib().fa_last_error()
+    assert L.lib().fa_bwd_noalloc(C.byref(bp), None) == L.FA_ERR_INVALID
+    assert L.lib().fa_last_error() == msg and b"static scratch" not in msg
+    bp.H_kv = 0
+    assert L.lib().fa_bwd_noalloc(C.byref(bp), None) == L.FA_ERR_INVALID
+    assert b"H_kv=0" in L.lib().fa_last_error()
 
 
 def test_decode_validation_without_gpu():
