@@ -3,8 +3,8 @@
 //   bwd_preprocess  delta = rowsum(O * dO) in fp32 (reference:
 //                   flash_attention_bwd_preprocess_kernel, src/pallas_flexattn/
 //                   flash_attn.py:168-173, which stores it in O's dtype) and
-//                   lse2 = lse * log2(e); the fp32 dQ accumulator is zeroed by a
-//                   memset on the same stream.
+//                   lse2 = lse * log2(e); the same kernel zeroes the fp32 dQ
+//                   accumulator (a memset on the same stream for the generic shapes).
 //   dq_convert      dQ = scale * dq_accum, cast to the input dtype.
 //   lse_merge       combine two partial (O, logsumexp) results over disjoint keys.
 // bf16 rows of 64 or 128 elements (16-byte aligned) take the vector kernels: a few
@@ -117,32 +117,51 @@ __global__ void __launch_bounds__(kRowsPerCta * 32)
 
 constexpr int kVecPasses = 4;  // rows per lane group in flight
 
-// Vector preprocess for bf16 rows of D = 64 or 128: L = D / 8 lanes per row (16 bytes
-// each), 32 / L rows per pass, kVecPasses passes per warp, one warp-row group per pass.
+// Vector preprocess for bf16 rows of D = 64 or 128, fused with the zeroing of the fp32 dQ
+// accumulator.  One CTA per (64-row block, b*h): no per-row index division, every load of
+// the block issued before the first use (L = D / 8 lanes per row, 16 bytes each), delta and
+// lse2 staged in shared memory and stored as two coalesced 256-byte rows, and the block's
+// accumulator rows [bh, t0 .. t0+63, :] zeroed with coalesced 16-byte stores.  HBM traffic
+// per row: reads 2*D*2 bytes (o, dO) + 4 (lse), writes D*4 (zeros) + 8 (delta, lse2).
+constexpr int kPreRows = 64;
+
 template <int D>
-__global__ void __launch_bounds__(256) preprocess_bf16_vec_kernel(const AttnArgs a) {
-  constexpr int L = D / 8, RPP = 32 / L, RPW = RPP * kVecPasses;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane / L, li = lane % L;
-  const int64_t prows = (int64_t)a.B * a.H * a.Tq_pad;
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * RPW;
-  uint4 ov[kVecPasses], gv[kVecPasses];
+__global__ void __launch_bounds__(256) preprocess_bf16_zero_kernel(const AttnArgs a) {
+  constexpr int L = D / 8, RPP = 256 / L, NP = kPreRows / RPP;
+  __shared__ float s_delta[kPreRows];
+  __shared__ float s_lse[kPreRows];
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int t0 = blockIdx.x * kPreRows;
+  const int tid = threadIdx.x, sub = tid / L, li = tid % L;
+  const __nv_bfloat16* obase = reinterpret_cast<const __nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
+                               (int64_t)h * a.o.stride_h + li * 8;
+  const __nv_bfloat16* gbase = reinterpret_cast<const __nv_bfloat16*>(a.dout.ptr) + (int64_t)b * a.dout.stride_b +
+                               (int64_t)h * a.dout.stride_h + li * 8;
+  uint4 ov[NP], gv[NP];
 #pragma unroll
-  for (int p = 0; p < kVecPasses; ++p) {
-    const int64_t prow = row0 + p * RPP + sub;
-    const int t = (int)(prow % a.Tq_pad);
-    const int bh = (int)(prow / a.Tq_pad), b = bh / a.H, h = bh % a.H;
+  for (int p = 0; p < NP; ++p) {
+    const int t = t0 + p * RPP + sub;
     ov[p] = gv[p] = make_uint4(0u, 0u, 0u, 0u);
-    if (prow < prows && t < a.Tq) {
-      ov[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
-                                              (int64_t)h * a.o.stride_h + (int64_t)t * a.o.stride_t + li * 8);
-      gv[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.dout.ptr) +
-                                              (int64_t)b * a.dout.stride_b + (int64_t)h * a.dout.stride_h +
-                                              (int64_t)t * a.dout.stride_t + li * 8);
+    if (t < a.Tq) {
+      ov[p] = __ldg(reinterpret_cast<const uint4*>(obase + (int64_t)t * a.o.stride_t));
+      gv[p] = __ldg(reinterpret_cast<const uint4*>(gbase + (int64_t)t * a.dout.stride_t));
+    }
+  }
+  if (a.lse2 && tid < kPreRows) {
+    const int t = t0 + tid;
+    s_lse[tid] = t < a.Tq ? __ldg(a.lse_in + (int64_t)bh * a.Tq + t) : -INFINITY;
+  }
+  // zero the block's rows of the dQ accumulator ([B*H, Tq, D]; rows past Tq do not exist)
+  {
+    const int nrows = min(kPreRows, a.Tq - t0);
+    if (nrows > 0) {
+      float4* z = reinterpret_cast<float4*>(a.dq_accum + ((int64_t)bh * a.Tq + t0) * D);
+      const int n4 = nrows * (D / 4);
+      for (int i = tid; i < n4; i += 256) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 #pragma unroll
-  for (int p = 0; p < kVecPasses; ++p) {
+  for (int p = 0; p < NP; ++p) {
     const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[p]);
     const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[p]);
     float acc = 0.f;
@@ -153,16 +172,16 @@ __global__ void __launch_bounds__(256) preprocess_bf16_vec_kernel(const AttnArgs
     }
 #pragma unroll
     for (int off = L / 2; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    const int64_t prow = row0 + p * RPP + sub;
-    if (li == 0 && prow < prows) {
-      const int t = (int)(prow % a.Tq_pad);
-      const int64_t row = (prow / a.Tq_pad) * a.Tq + t;
-      a.delta[prow] = t < a.Tq ? acc : 0.f;
-      if (a.lse2) {
-        const float l = t < a.Tq ? a.lse_in[row] : -INFINITY;
-        a.lse2[prow] = (l == -INFINITY) ? INFINITY : l * kLog2e;
-      }
-    }
+    if (li == 0) s_delta[p * RPP + sub] = acc;  // 0 for rows past Tq (their loads were zeros)
+  }
+  __syncthreads();
+  if (tid < kPreRows) {
+    const int t = t0 + tid;
+    if (t < a.Tq_pad) a.delta[(int64_t)bh * a.Tq_pad + t] = s_delta[tid];
+  } else if (a.lse2 && tid < 2 * kPreRows) {
+    const int r = tid - kPreRows, t = t0 + r;
+    const float l = s_lse[r];
+    if (t < a.Tq_pad) a.lse2[(int64_t)bh * a.Tq_pad + t] = (l == -INFINITY) ? INFINITY : l * kLog2e;
   }
 }
 
@@ -207,18 +226,18 @@ bool rows16(const FaTensor& t, int elem_bytes) {
 
 cudaError_t launch_bwd_preprocess(const AttnArgs& a, int dtype, cudaStream_t stream) {
   const int64_t rows = (int64_t)a.B * a.H * a.Tq_pad;
+  const bool vec = dtype == FA_DTYPE_BF16 && (a.D == 64 || a.D == 128) && rows16(a.o, 2) && rows16(a.dout, 2) &&
+                   (reinterpret_cast<uintptr_t>(a.dq_accum) % 16 == 0);
+  if (vec) {  // the kernel zeroes the dQ accumulator itself
+    const dim3 grid((unsigned)((a.Tq_pad + kPreRows - 1) / kPreRows), (unsigned)(a.B * a.H));
+    if (a.D == 128) preprocess_bf16_zero_kernel<128><<<grid, 256, 0, stream>>>(a);
+    else preprocess_bf16_zero_kernel<64><<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   // The dQ accumulator: B*H*Tq_pad*D floats (all of it in the padded layout of fa_bwd,
   // exactly [B*H, Tq, D] in the public preprocess entry point, where Tq_pad = Tq).
   cudaError_t e = cudaMemsetAsync(a.dq_accum, 0, (size_t)rows * a.D * sizeof(float), stream);
   if (e != cudaSuccess) return e;
-  const bool vec = dtype == FA_DTYPE_BF16 && (a.D == 64 || a.D == 128) && rows16(a.o, 2) && rows16(a.dout, 2);
-  if (vec) {
-    const int64_t per_cta = 8LL * kVecPasses * (32 / (a.D / 8));
-    const unsigned grid = (unsigned)((rows + per_cta - 1) / per_cta);
-    if (a.D == 128) preprocess_bf16_vec_kernel<128><<<grid, 256, 0, stream>>>(a);
-    else preprocess_bf16_vec_kernel<64><<<grid, 256, 0, stream>>>(a);
-    return cudaGetLastError();
-  }
   const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
   if (dtype == FA_DTYPE_F32) preprocess_kernel<float><<<grid, kRowsPerCta * 32, 0, stream>>>(a);
   else preprocess_kernel<__nv_bfloat16><<<grid, kRowsPerCta * 32, 0, stream>>>(a);

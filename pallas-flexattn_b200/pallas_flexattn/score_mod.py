@@ -144,3 +144,23 @@ def compose_score_mods(*mods: ScoreMod) -> ScoreMod:
     score_mod.__fa_spec__ = ScoreSpec(flags=flags, softcap=cap, alibi_slopes=slopes, rel_bias=bias)
     return score_mod
 
+
+
+def slice_heads(score_mod: Optional[ScoreMod], h0: int, h1: int) -> Optional[ScoreMod]:
+    """The same registry score_mod restricted to heads [h0, h1): per-head ALiBi slopes and
+    relative-bias rows are sliced, head-independent parts are kept.  For head-sharded
+    execution, where a rank runs heads h0..h1-1 of the full problem as its heads 0..h1-h0-1."""
+    spec = spec_of(score_mod)
+    if spec is None:
+        raise NotImplementedError("slice_heads: the score_mod has no registry entry")
+    if spec.flags == 0:
+        return score_mod
+    parts = []
+    if spec.flags & L.FA_SCORE_ALIBI:
+        parts.append(alibi_score_mod(slopes=spec.alibi_slopes[h0:h1]))
+    if spec.flags & L.FA_SCORE_REL_BIAS:
+        bias = spec.rel_bias if spec.rel_bias.shape[0] == 1 else spec.rel_bias[h0:h1]
+        parts.append(relative_bias_score_mod(bias))
+    if spec.flags & L.FA_SCORE_SOFTCAP:
+        parts.append(softcap_score_mod(spec.softcap))
+    return parts[0] if len(parts) == 1 else compose_score_mods(*parts)

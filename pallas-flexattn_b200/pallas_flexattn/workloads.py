@@ -12,14 +12,14 @@ lengths and the random tile table are drawn with numpy's default_rng(seed):
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 from typing import Callable, Optional
 
 import numpy as np
 import torch
 
 from .mask_mod import and_masks, causal_mask, document_mask, sliding_window_mask, tile_mask
-from .score_mod import alibi_score_mod, softcap_score_mod
+from .score_mod import alibi_score_mod, slice_heads, softcap_score_mod
 
 
 def document_lengths(S: int, seed: int = 0, lo: int = 256, hi: int = 4096) -> list[int]:
@@ -66,6 +66,17 @@ class Workload:
             t = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * self.input_scale
             out.append(t.to(self.dtype))
         return out
+
+    def head_shard(self, rank: int, world: int) -> "Workload":
+        """Rank `rank`'s share of the problem when its H heads are split evenly over `world`
+        ranks (heads are independent: no exchange is needed).  Per-head score parameters
+        (ALiBi slopes) follow their heads."""
+        if self.H % world:
+            raise ValueError(f"{self.name}: H={self.H} heads do not split over {world} ranks")
+        n = self.H // world
+        h0 = rank * n
+        return replace(self, H=n, score_mod=slice_heads(self.score_mod, h0, h0 + n),
+                       extra={**self.extra, "heads": (h0, h0 + n), "full_H": self.H})
 
     def fwd_flops(self, n_pairs: int, B: Optional[int] = None, H: Optional[int] = None) -> float:
         """Effective forward FLOPs: 4 * D * unmasked pairs per (b, h) * B * H."""

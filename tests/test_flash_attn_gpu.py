@@ -345,3 +345,31 @@ def test_benchmark_config_full_length(cfg, seed):
     for n, a, b in zip(("o", "lse", "dq", "dk", "dv"), (o, None, dq, dk, dv), ref):
         if a is not None:
             close(n, a, b, torch.bfloat16)
+
+
+@pytest.mark.parametrize("D,T", [(128, 1000), (64, 4097), (96, 300)])
+def test_bwd_preprocess_entry_point(D, T):
+    """fa_bwd_preprocess: delta = rowsum(o * dO) in fp32 for every row, and the dQ accumulator
+    [B*H, T, D] zeroed (it starts full of garbage here)."""
+    import ctypes as C
+
+    from pallas_flexattn import _lib as L
+    from pallas_flexattn import flash_attn as FA
+
+    q, k, v, do = inputs((2, 3, T, D), (2, 3, T, D), torch.bfloat16, seed=T)
+    o = torch.randn_like(q.float()).to(torch.bfloat16)
+    lse = torch.zeros(q.shape[:3], dtype=torch.float32, device=DEV)
+    plan = FA._Plan(q, k, v, pf.causal_mask, None, None, 64, 64, 3, None, True)
+    p = L.FaBwdParams()
+    plan._fill(p)
+    p.q, p.k, p.v, p.o, p.dout = (FA._fa_tensor(t) for t in (q, k, v, o, do))
+    p.dq, p.dk, p.dv = (FA._fa_tensor(torch.empty_like(t)) for t in (q, k, v))
+    p.lse = lse.data_ptr()
+    delta = torch.full((2 * 3 * T,), float("nan"), dtype=torch.float32, device=DEV)
+    acc = torch.full((2 * 3 * T * D,), 7.0, dtype=torch.float32, device=DEV)
+    L.check(L.lib().fa_bwd_preprocess(C.byref(p), delta.data_ptr(), acc.data_ptr(),
+                                      torch.cuda.current_stream(DEV).cuda_stream))
+    torch.cuda.synchronize()
+    ref = (o.float() * do.float()).sum(-1).flatten()
+    torch.testing.assert_close(delta, ref, atol=1e-4, rtol=1e-5)
+    assert int((acc != 0).sum()) == 0
