@@ -473,6 +473,106 @@ def measure_config(cfg: int, dist, rank: int, world: int, device, steps: int, pe
     return res
 
 
+def measure_cp_ring(dist, rank: int, world: int, device, steps: int, peak: float, timer: StepTimer,
+                    cfg: int = 5) -> dict:
+    """The config (default cfg5) as context-parallel ring attention over the ranks: each rank
+    holds its zig-zag share of the sequence for every head, K/V (and in the backward the
+    fp32 dK/dV accumulators) travel the ring on NCCL send/recv.  Whole-problem effective
+    TFLOP/s of the ring forward and backward, the exchange time of one step's K/V block
+    against the compute per step, and parity of one head's full sequence against fp32."""
+    from pallas_flexattn import ring
+    from pallas_flexattn import workloads as W
+    from pallas_flexattn.score_mod import slice_heads
+
+    wf = W.get(cfg)
+    n_pairs = W.count_pairs(wf.mask_mod, wf.S, wf.S, device=device)
+    fwd_flops = wf.fwd_flops(n_pairs)
+    T2 = wf.S // world
+    g = torch.Generator(device=device).manual_seed(500 + rank)
+    q, k, v, do = (torch.randn((wf.B, wf.H, T2, wf.D), generator=g, device=device).to(wf.dtype) for _ in range(4))
+    grp = dist.group.WORLD if dist is not None else None
+    if dist is None:  # one GPU: a single-rank process group keeps the ring code path
+        import torch.distributed as tdist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29600 + os.getpid() % 1000))
+        tdist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=120))
+        grp = tdist.group.WORLD
+    o, lse = ring.ring_attention_fwd(q, k, v, wf.mask_mod, wf.score_mod, group=grp)
+
+    def fwd():
+        return ring.ring_attention_fwd(q, k, v, wf.mask_mod, wf.score_mod, group=grp)
+
+    def bwd():
+        return ring.ring_attention_bwd(q, k, v, o, lse, do, wf.mask_mod, wf.score_mod, group=grp)
+
+    for _ in range(2):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    ms_f = timer.run(dist, fwd, steps)
+    ms_b = timer.run(dist, bwd, steps)
+    # one step's K/V exchange alone (the bytes the forward moves per step), for the limiter
+    ms_x = None
+    kv_bytes = 2 * q.numel() * q.element_size()
+    if world > 1:
+        import torch.distributed as tdist
+
+        nk, nv = torch.empty_like(k), torch.empty_like(v)
+        nxt, prv = (rank + 1) % world, (rank - 1) % world
+
+        def exchange():
+            ops = [tdist.P2POp(tdist.isend, k, nxt), tdist.P2POp(tdist.isend, v, nxt),
+                   tdist.P2POp(tdist.irecv, nk, prv), tdist.P2POp(tdist.irecv, nv, prv)]
+            for w_ in tdist.batch_isend_irecv(ops):
+                w_.wait()
+
+        exchange()
+        ms_x = timer.run(dist, exchange, steps)
+    res = {"workload": wf.name, "strategy": f"zig-zag K/V ring over {world} GPU(s), {2 * world} chunks of "
+                                            f"{wf.S // (2 * world)} rows, all {wf.H} heads per GPU",
+           "fwd": {"ms": ms_f, "tflops": fwd_flops / (ms_f * 1e-3) / 1e12,
+                   "pct_of_peak": 100 * fwd_flops / (ms_f * 1e-3) / 1e12 / world / peak},
+           "bwd": {"ms": ms_b, "tflops": 2.5 * fwd_flops / (ms_b * 1e-3) / 1e12,
+                   "pct_of_peak": 100 * 2.5 * fwd_flops / (ms_b * 1e-3) / 1e12 / world / peak},
+           "kv_bytes_per_step": kv_bytes, "exchange_ms_per_step": ms_x,
+           "compute_ms_per_step": {"fwd": ms_f / world, "bwd": ms_b / world},
+           "exchange_GBps": (kv_bytes / (ms_x * 1e-3) / 1e9) if ms_x else None}
+    if ms_x is not None:
+        res["limiter"] = ("K/V exchange (NCCL send/recv)" if ms_x > ms_f / world else "compute per step")
+    del q, k, v, do, o, lse
+    torch.cuda.empty_cache()
+    # parity: one head, the full sequence generated identically on every rank and split zig-zag
+    g1 = torch.Generator(device=device).manual_seed(77)
+    full = [torch.randn((1, 1, wf.S, wf.D), generator=g1, device=device).to(wf.dtype) for _ in range(4)]
+    sm = slice_heads(wf.score_mod, 0, 1)
+    mine = [ring.split_zigzag(t, rank, world).contiguous() for t in full]
+    qq, kk, vv = (t.clone().requires_grad_(True) for t in mine[:3])
+    o1 = ring.ring_attention(qq, kk, vv, wf.mask_mod, sm, group=grp)
+    got = (o1.detach(), *torch.autograd.grad(o1, (qq, kk, vv), mine[3]))
+    gathered = []
+    for t in got:
+        if world > 1:
+            import torch.distributed as tdist
+
+            bufs = [torch.empty_like(t) for _ in range(world)]
+            tdist.all_gather(bufs, t.contiguous())
+            gathered.append(ring.gather_zigzag(bufs, world))
+        else:
+            gathered.append(ring.gather_zigzag([t], 1))
+    if rank == 0:
+        ref = reference_fwd_bwd(*full, wf.mask_mod, sm, chunk=512)
+        par = {n: parity_stats(a, r_, True) for n, a, r_ in zip(("o", "dq", "dk", "dv"), gathered, ref)}
+        par["slice"] = "head 0 of a separate seeded input, the whole sequence gathered from the ring"
+        par["pass"] = all(par[n]["pass"] for n in ("o", "dq", "dk", "dv"))
+        res["parity"] = par
+    if dist is None:
+        import torch.distributed as tdist
+
+        tdist.destroy_process_group()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -590,6 +690,10 @@ def main():
                 r["rate_vs_cfg2_per_unmasked_flop"] = {
                     "fwd": r["fwd"]["tflops"] / ref2["fwd"]["tflops"], "bwd": r["bwd"]["tflops"] / ref2["bwd"]["tflops"]}
 
+    cp_ring = None
+    if not args.no_per_config:
+        cp_ring = measure_cp_ring(dist, rank, world, device, max(3, args.steps // 4), peak, timer)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, n_pairs)
@@ -621,6 +725,7 @@ def main():
             "gpu_launches": args.steps * (fwd_launches + bwd_launches),
             "parity": parity,
             "per_config": per_config,
+            "cp_ring": cp_ring,
             "block_mask_ms": bm_ms,
             "comparators": comparators,
             "unmasked_pairs_per_bh": n_pairs,

@@ -1,4 +1,4 @@
-"""Context-parallel (ring) attention forward for long sequences.
+"""Context-parallel (ring) attention for long sequences: forward, backward and autograd.
 
 The sequence is cut into 2·W chunks of equal length (W = world size) and rank r
 owns chunks r and 2W-1-r ("zig-zag", which balances causal work across ranks).
@@ -12,10 +12,21 @@ Each rank keeps its Q chunks and passes its K/V chunks around the ring:
                         and merge the partial (o, lse) into fp32 accumulators
                         (log-sum-exp combine, ``fa_lse_merge``)
 
+The backward (``ring_attention_bwd``) walks the same ring.  Each rank keeps its Q,
+O, dO and the final logsumexp rows and accumulates dQ locally in fp32; the K/V
+blocks travel as in the forward, and with each block travel its fp32 dK/dV
+accumulators.  At step s a rank adds the contributions of its Q chunks to the
+held block (one fused backward call per unmasked chunk pair, the mask and score
+mods at global positions, P recomputed from the final logsumexp) into a local
+buffer, adds the accumulators that arrive from the previous rank, and sends the
+sum on to the next rank; after the last step the accumulators have gone round
+the ring once and arrive back at the block's owner.  The accumulator exchange of
+step s overlaps the compute of step s+1.
+
 On GPUs the exchange is NCCL send/recv through ``torch.distributed`` (NVLink) on
 NCCL's own stream, overlapped with the attention kernels on the compute stream.
-The partial-attention and merge functions are injectable so the same schedule
-runs on CPU ranks (gloo) in tests.
+The partial-attention, partial-gradient and merge functions are injectable so the
+same schedule runs on CPU ranks (gloo) in tests.
 """
 from __future__ import annotations
 
@@ -128,14 +139,17 @@ def ring_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_m
     q_parts = (q[:, :, :Cl], q[:, :, Cl:])
     o_acc = [torch.zeros((B, H, Cl, D), dtype=torch.float32, device=q.device) for _ in range(2)]
     lse_acc = [torch.full((B, H, Cl), -math.inf, dtype=torch.float32, device=q.device) for _ in range(2)]
+    # The caller's k/v are only read (sent at step 0); received blocks alternate between two
+    # buffers of the ring's own, so no receive ever writes a caller tensor.
     cur_k, cur_v = k.contiguous(), v.contiguous()
-    nxt_k, nxt_v = torch.empty_like(cur_k), torch.empty_like(cur_v)
+    bufs = [(torch.empty_like(cur_k), torch.empty_like(cur_v)) for _ in range(2 if world > 2 else 1)]
     nxt_rank, prv_rank = (rank + 1) % world, (rank - 1) % world
     g = dist.get_global_rank(group, nxt_rank) if group is not None else nxt_rank
     gp = dist.get_global_rank(group, prv_rank) if group is not None else prv_rank
     for s in range(world):
         works = []
         if s + 1 < world:
+            nxt_k, nxt_v = bufs[s % len(bufs)]
             ops = [dist.P2POp(dist.isend, cur_k, g, group), dist.P2POp(dist.isend, cur_v, g, group),
                    dist.P2POp(dist.irecv, nxt_k, gp, group), dist.P2POp(dist.irecv, nxt_v, gp, group)]
             works = dist.batch_isend_irecv(ops)
@@ -157,8 +171,123 @@ def ring_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_m
         for w_ in works:
             w_.wait()
         if s + 1 < world:
-            cur_k, nxt_k = nxt_k, cur_k
-            cur_v, nxt_v = nxt_v, cur_v
+            cur_k, cur_v = nxt_k, nxt_v
         if stats:
             stats.steps += 1
     return torch.cat(o_acc, dim=2).to(q.dtype), torch.cat(lse_acc, dim=2)
+
+
+def gpu_partial_attention_bwd(q, k, v, o, lse, do, mask_mod, score_mod, q_offset: int, kv_offset: int):
+    """(dq, dk, dv) contributions of one (q chunk, K/V chunk) pair, on the fused tcgen05
+    backward: P is recomputed from the final logsumexp `lse` and delta from the final `o`."""
+    from .flash_attn import _Plan, _run_bwd
+
+    plan = _Plan(q, k, v, mask_mod, score_mod, None, 64, 64, 0, None, need_bwd=True,
+                 offsets=(q_offset, kv_offset))
+    return _run_bwd(plan, q, k, v, o, lse, do)
+
+
+def ring_attention_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, lse: torch.Tensor,
+                       do: torch.Tensor, mask_mod=None, score_mod=None, *, group=None,
+                       attn_bwd_fn: Optional[Callable] = None, pair_is_empty: Optional[Callable] = None,
+                       stats: Optional[RingStats] = None):
+    """Gradients of ring attention over the process group.  q, k, v, o and do hold this rank's
+    zig-zag share ([B, H(_kv), 2C, D]), lse its fp32 logsumexp rows ([B, H, 2C]), both from
+    ring_attention_fwd.  Returns (dq, dk, dv) for the rank's share, in the input dtypes."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    attn_bwd_fn = attn_bwd_fn or gpu_partial_attention_bwd
+    pair_is_empty = pair_is_empty or _default_pair_is_empty
+    B, H, T2, D = q.shape
+    Cl = T2 // 2
+    if 2 * Cl != T2 or k.shape[2] != T2 or tuple(o.shape) != tuple(q.shape) or tuple(do.shape) != tuple(q.shape):
+        raise ValueError("q/k/v/o/do must hold two equal chunks")
+    my = zigzag_chunks(rank, world)
+    halves = lambda x: (x[:, :, :Cl], x[:, :, Cl:])  # noqa: E731
+    q_p, o_p, do_p = halves(q), halves(o), halves(do)
+    lse = lse.to(torch.float32)
+    l_p = (lse[:, :, :Cl], lse[:, :, Cl:])
+    dq_acc = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    cur_k, cur_v = k.contiguous(), v.contiguous()  # read only; received blocks go to the ring's buffers
+    bufs = [(torch.empty_like(cur_k), torch.empty_like(cur_v)) for _ in range(2 if world > 2 else 1)]
+    nxt_rank, prv_rank = (rank + 1) % world, (rank - 1) % world
+    g = dist.get_global_rank(group, nxt_rank) if group is not None else nxt_rank
+    gp = dist.get_global_rank(group, prv_rank) if group is not None else prv_rank
+    acc_works, acc_send, acc_recv = [], None, None
+    for s in range(world):
+        kv_works = []
+        if s + 1 < world:
+            nxt_k, nxt_v = bufs[s % len(bufs)]
+            ops = [dist.P2POp(dist.isend, cur_k, g, group), dist.P2POp(dist.isend, cur_v, g, group),
+                   dist.P2POp(dist.irecv, nxt_k, gp, group), dist.P2POp(dist.irecv, nxt_v, gp, group)]
+            kv_works = dist.batch_isend_irecv(ops)
+        held = zigzag_chunks((rank - s) % world, world)
+        dk_loc = torch.zeros(cur_k.shape, dtype=torch.float32, device=k.device)
+        dv_loc = torch.zeros(cur_v.shape, dtype=torch.float32, device=v.device)
+        for qi, qc in enumerate(my):
+            for ki, kc in enumerate(held):
+                q0, k0 = qc * Cl, kc * Cl
+                if pair_is_empty(mask_mod, q0, q0 + Cl, k0, k0 + Cl):
+                    if stats:
+                        stats.pairs_skipped += 1
+                    continue
+                ks = slice(ki * Cl, (ki + 1) * Cl)
+                dq_c, dk_c, dv_c = attn_bwd_fn(q_p[qi], cur_k[:, :, ks], cur_v[:, :, ks], o_p[qi], l_p[qi], do_p[qi],
+                                               mask_mod, score_mod, q0, k0)
+                dq_acc[:, :, qi * Cl:(qi + 1) * Cl] += dq_c.float()
+                dk_loc[:, :, ks] += dk_c.float()
+                dv_loc[:, :, ks] += dv_c.float()
+                if stats:
+                    stats.pairs_computed += 1
+        if world > 1:
+            if s > 0:  # the held block's accumulators, sent on by the previous rank after its step s-1
+                for w_ in acc_works:
+                    w_.wait()
+                dk_loc += acc_recv[0]
+                dv_loc += acc_recv[1]
+            acc_send = (dk_loc, dv_loc)  # referenced until the sends complete
+            acc_recv = (torch.empty_like(dk_loc), torch.empty_like(dv_loc))
+            # tag 1 keeps these apart from the K/V messages (tag 0) of the same step on backends
+            # that match by tag (gloo); NCCL matches in posting order, which is the same on all ranks
+            ops = [dist.P2POp(dist.isend, acc_send[0], g, group, tag=1),
+                   dist.P2POp(dist.isend, acc_send[1], g, group, tag=1),
+                   dist.P2POp(dist.irecv, acc_recv[0], gp, group, tag=1),
+                   dist.P2POp(dist.irecv, acc_recv[1], gp, group, tag=1)]
+            acc_works = dist.batch_isend_irecv(ops)
+        else:
+            acc_recv = (dk_loc, dv_loc)
+        for w_ in kv_works:
+            w_.wait()
+        if s + 1 < world:
+            cur_k, cur_v = nxt_k, nxt_v
+        if stats:
+            stats.steps += 1
+    for w_ in acc_works:  # the own block's accumulators, back from the last holder
+        w_.wait()
+    del acc_send
+    return dq_acc.to(q.dtype), acc_recv[0].to(k.dtype), acc_recv[1].to(v.dtype)
+
+
+class _RingAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, mask_mod, score_mod, group):
+        o, lse = ring_attention_fwd(q, k, v, mask_mod, score_mod, group=group)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.cfg = (mask_mod, score_mod, group)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        mask_mod, score_mod, group = ctx.cfg
+        dq, dk, dv = ring_attention_bwd(q, k, v, o, lse, do.contiguous(), mask_mod, score_mod, group=group)
+        return dq, dk, dv, None, None, None
+
+
+def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_mod=None, score_mod=None, *,
+                   group=None) -> torch.Tensor:
+    """Differentiable context-parallel attention: this rank's zig-zag share of the output;
+    the backward runs ring_attention_bwd."""
+    return _RingAttentionFn.apply(q, k, v, mask_mod, score_mod, group)

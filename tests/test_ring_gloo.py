@@ -1,10 +1,11 @@
-"""Context-parallel ring schedule on CPU ranks (gloo), world sizes 2 and 3.
+"""Context-parallel ring schedule on CPU ranks (gloo), world sizes 2 and 3, forward and backward.
 
 The ring (pallas_flexattn/ring.py) takes its partial-attention and merge functions as
 arguments; here they are an fp64 torch reference with global-position masks and the torch
 log-sum-exp merge, so the test covers the schedule itself: zig-zag ownership, the K/V
 exchange, skipping of fully masked chunk pairs and the merge order.  The result is compared
-with full-sequence attention.  A fault test makes one rank raise before the ring starts and
+with full-sequence attention; the backward (K/V and the travelling dK/dV accumulators)
+with fp64 autograd through full-sequence attention.  A fault test makes one rank raise before the ring starts and
 checks that its peer fails with an error (process-group timeout) instead of hanging.
 """
 import datetime
@@ -41,6 +42,31 @@ def ref_partial(q, k, v, mask_mod, score_mod, q_offset, kv_offset):
     p = torch.where(torch.isfinite(lse)[..., None], torch.exp(s - lse[..., None]), torch.zeros_like(s))
     o = torch.einsum("bhqk,bhkd->bhqd", p, vd)
     return o.float(), lse.float()
+
+
+def ref_partial_bwd(q, k, v, o, lse, do, mask_mod, score_mod, q_offset, kv_offset):
+    """(dq, dk, dv) of one chunk pair in fp64 from the final o and lse, masks at global positions."""
+    del score_mod
+    qd, kd, vd, od, dod = (t.double() for t in (q, k, v, o, do))
+    sc = 1.0 / math.sqrt(q.shape[-1])
+    s = torch.einsum("bhqd,bhkd->bhqk", qd, kd) * sc
+    qi = torch.arange(q.shape[2])[:, None] + q_offset
+    ki = torch.arange(k.shape[2])[None, :] + kv_offset
+    allowed = torch.ones_like(qi >= ki) if mask_mod is None else torch.broadcast_to(mask_mod(qi, ki), s.shape[-2:])
+    lse = lse.double()
+    p = torch.where(allowed & torch.isfinite(lse)[..., None], torch.exp(s - lse[..., None]), torch.zeros_like(s))
+    delta = (od * dod).sum(-1, keepdim=True)
+    ds = p * (torch.einsum("bhqd,bhkd->bhqk", dod, vd) - delta)
+    return ((ds @ kd) * sc).float(), ((ds.transpose(-1, -2) @ qd) * sc).float(), (p.transpose(-1, -2) @ dod).float()
+
+
+def full_attention_fp64(q, k, v, mask_mod):
+    s = torch.einsum("bhqd,bhkd->bhqk", q, k) / math.sqrt(q.shape[-1])
+    T = q.shape[2]
+    if mask_mod is not None:
+        s = s.masked_fill(~torch.broadcast_to(mask_mod(torch.arange(T)[:, None], torch.arange(T)[None, :]),
+                                              s.shape[-2:]), -math.inf)
+    return torch.softmax(s, -1).nan_to_num(0.0) @ v
 
 
 MASKS = {
@@ -93,6 +119,52 @@ def test_ring_matches_full_attention(tmp_path, world, mask_name):
     assert r["computed"] + r["skipped"] == 4 * world
     if mask_name == "causal":
         assert r["skipped"] > 0  # kv chunks after both of rank 0's q chunks are never computed
+
+
+def _bwd_worker(rank, world, port, mask_name, out_dir):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        T = 12 * world
+        g = torch.Generator().manual_seed(1)
+        q, k, v, do = (torch.randn(1, 2, T, 8, generator=g) for _ in range(4))
+        mask_mod = MASKS[mask_name](T)
+        mine = [ring.split_zigzag(x, rank, world) for x in (q, k, v, do)]
+        before = [t.clone() for t in mine]
+        o, lse = ring.ring_attention_fwd(*mine[:3], mask_mod, attn_fn=ref_partial, merge_fn=ring.torch_merge)
+        stats = ring.RingStats()
+        dq, dk, dv = ring.ring_attention_bwd(*mine[:3], o, lse, mine[3], mask_mod, attn_bwd_fn=ref_partial_bwd,
+                                             stats=stats)
+        # the exchange receives into the ring's own buffers: the caller's tensors are only read
+        untouched = all(torch.equal(a, b) for a, b in zip(mine, before))
+        parts = {}
+        for name, t in (("dq", dq), ("dk", dk), ("dv", dv)):
+            bufs = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(bufs, t)
+            parts[name] = ring.gather_zigzag(bufs, world)
+        if rank == 0:
+            qd, kd, vd = (t.double().requires_grad_(True) for t in (q, k, v))
+            ref = torch.autograd.grad(full_attention_fp64(qd, kd, vd, mask_mod), (qd, kd, vd), do.double())
+            torch.save({**parts, "ref": [r.float() for r in ref], "steps": stats.steps,
+                        "computed": stats.pairs_computed, "untouched": untouched},
+                       os.path.join(out_dir, "result.pt"))
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(out_dir, f"error{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("mask_name", ["causal", "window", "document"])
+def test_ring_backward_matches_full_attention(tmp_path, world, mask_name):
+    mp.start_processes(_bwd_worker, args=(world, _free_port(), mask_name, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    r = torch.load(tmp_path / "result.pt")
+    for i, name in enumerate(("dq", "dk", "dv")):
+        torch.testing.assert_close(r[name], r["ref"][i], atol=1e-5, rtol=1e-5, msg=name)
+    assert r["steps"] == world and r["computed"] > 0
+    assert r["untouched"], "the ring wrote into the caller's q/k/v/dO"
 
 
 def test_zigzag_round_trip():
