@@ -131,6 +131,16 @@ typedef struct {
   int64_t stride_b, stride_h, stride_t;
 } FaTensor;
 
+/* Launch shape of the tcgen05 forward (FaFwdParams.tile_cfg), the measured autotuner's
+ * choices besides the pipeline depth.  Bits 0-1: Q tiles per CTA; bits 2-3: softmax schedule
+ * of the two softmax warpgroups.  0 in a field = the launcher's per-launch choice. */
+enum {
+  FA_TILE_Q2 = 1,                 /* two 128-row Q tiles per CTA sharing each K/V tile load */
+  FA_TILE_Q1 = 2,                 /* one Q tile per CTA (twice the CTAs; for small grids) */
+  FA_TILE_SOFTMAX_CONCURRENT = 4, /* both softmax warpgroups run at once */
+  FA_TILE_SOFTMAX_TURNS = 8,      /* strict turns per kv tile (no score_mod only) */
+};
+
 typedef struct {
   int32_t dtype;            /* FA_DTYPE_BF16 or FA_DTYPE_F32; q/k/v/o share it */
   int32_t B, H, H_kv;       /* H_kv divides H (grouped-query attention when < H) */
@@ -145,6 +155,7 @@ typedef struct {
   int32_t num_stages;       /* K/V entries in flight in the tcgen05 forward (each = K + V tile);
                                0 = as many as shared memory holds */
   int32_t* status;          /* optional device int32: nonzero after a device-side timeout */
+  int32_t tile_cfg;         /* FA_TILE_* launch shape of the tcgen05 forward; 0 = chosen per launch */
 } FaFwdParams;
 
 typedef struct {
@@ -159,8 +170,9 @@ typedef struct {
   FaScoreSpec score;
   FaBlockTables blocks;
   int32_t kernel;
-  int32_t num_stages;
+  int32_t num_stages;       /* Q/dO tiles in flight in the tcgen05 backward; 0 = default (2) */
   int32_t* status;
+  int32_t tile_cfg;         /* reserved for launch-shape choices of the backward; pass 0 */
 } FaBwdParams;
 
 /* ------------------------------------------------------------------ entry points */

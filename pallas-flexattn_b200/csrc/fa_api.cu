@@ -198,7 +198,8 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
         (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")))
       return rc;
-    cudaError_t e = launch_fwd_tc(a, tq, tk, tv, (cudaStream_t)stream);
+    if (p->tile_cfg & ~15) return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
+    cudaError_t e = launch_fwd_tc(a, tq, tk, tv, p->tile_cfg, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_fwd (tcgen05)");
     return FA_OK;
   }

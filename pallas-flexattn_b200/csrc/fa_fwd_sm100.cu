@@ -82,7 +82,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv)
 template <int D, int SK>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int pingpong) {
+                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int pingpong, const int tpc) {
   constexpr int CHUNK_BYTES = kBM * 64 * 2;  // one 64-column, 128-byte-swizzled panel
   constexpr int NCHUNK = D / 64;
   constexpr uint32_t TM_S0 = 0, TM_O0 = 256;
@@ -114,9 +114,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   int* entries = reinterpret_cast<int*>(smem + L.ent_off);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int npairs = (a.bt.nq + 1) >> 1;
+  // tpc = Q tiles per CTA: 2 (sub-tiles 0 and 1 are q tiles 2u and 2u+1, sharing every K/V
+  // load) or 1 (q tile u only; sub-tile 1 gets the invalid index nq and idles, which doubles
+  // the CTAs for grids that would not fill the SMs).
+  const int nunits = tpc == 2 ? (a.bt.nq + 1) >> 1 : a.bt.nq;
   const int bh = blockIdx.x % (a.B * a.H);
-  const int pair = npairs - 1 - (int)(blockIdx.x / (a.B * a.H));  // heaviest (last) q rows first
+  const int unit = nunits - 1 - (int)(blockIdx.x / (a.B * a.H));  // heaviest (last) q rows first
+  const int qt0 = tpc == 2 ? 2 * unit : unit;
+  const int qt1 = tpc == 2 ? 2 * unit + 1 : a.bt.nq;
   const int b = bh / a.H, h = bh % a.H;
   const int hk = h / (a.H / a.Hkv);
 
@@ -154,7 +159,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   {
     const int64_t head = table_head(a.bt, b, h);
     for (int i = 0; i < 2; ++i) {
-      const int qt = 2 * pair + i;
+      const int qt = i ? qt1 : qt0;
       if (qt >= a.bt.nq) continue;
       const int64_t row = head * a.bt.nq + qt;
       const int np = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[row] : 0;
@@ -199,11 +204,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_ent > 0) {
-      const bool has1 = (2 * pair + 1) < a.bt.nq;
+      const bool has1 = qt1 < a.bt.nq;
       mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
       for (int i = 0; i < (has1 ? 2 : 1); ++i)
         for (int c = 0; c < NCHUNK; ++c)
-          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (2 * pair + i) * kBM, h, b);
+          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (i ? qt1 : qt0) * kBM, h, b);
       bool ok = true;
       int issued = 0;  // loads issued so far (K and V alternate)
       for (int t = 0; t < n_ent && ok; ++t) {
@@ -328,7 +333,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int i = warp >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
-    const int q_row = (2 * pair + i) * kBM + r;
+    const int q_row = (i ? qt1 : qt0) * kBM + r;
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
     const uint32_t tS = t_lane + TM_S0 + 128 * i;
     const uint32_t tO = t_lane + TM_O0 + D * i;
@@ -552,21 +557,34 @@ int fwd_tc_max_stages(int D, int nkv) {
 }
 
 cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          cudaStream_t stream) {
+                          int tile_cfg, cudaStream_t stream) {
   const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv).total;
   const int npairs = (a.bt.nq + 1) / 2;
-  const dim3 grid((unsigned)(npairs * a.B * a.H));
+  // Q tiles per CTA (tile_cfg bits 0-1): two unless asked otherwise, or unless pairs would
+  // leave most of the SMs idle and single tiles at least double the CTAs.
+  int tpc = (tile_cfg & 3) == FA_TILE_Q1 ? 1 : 2;
+  if ((tile_cfg & 3) == 0) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if ((int64_t)npairs * a.B * a.H * 2 <= sms && a.bt.nq > 1) tpc = 1;
+  }
+  const dim3 grid((unsigned)((tpc == 2 ? npairs : a.bt.nq) * a.B * a.H));
   const int sk = score_kind_of(a.score.flags);
   // Strict softmax turns pay off when the tensor cores bound the loop (head dim 128, no
   // score_mod, no per-element mask predicate); a heavier softmax runs better with both
-  // warpgroups in flight at once.
+  // warpgroups in flight at once.  tile_cfg bits 2-3 override the choice; with one Q tile
+  // per CTA there is no second warpgroup to take turns with.
 #if FA_FWD_PINGPONG < 0
   const bool per_elem = (a.mask.flags & FA_MASK_TILE_TABLE) ||
                         ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
-  const int pingpong = a.D == 128 && sk == SC_NONE && !per_elem;
+  int pingpong = a.D == 128 && sk == SC_NONE && !per_elem;
+  if ((tile_cfg & 12) == FA_TILE_SOFTMAX_CONCURRENT) pingpong = 0;
+  if ((tile_cfg & 12) == FA_TILE_SOFTMAX_TURNS) pingpong = sk == SC_NONE;  // compiled only without a score_mod
 #else
-  const int pingpong = FA_FWD_PINGPONG;
+  int pingpong = FA_FWD_PINGPONG;
 #endif
+  if (tpc == 1) pingpong = 0;
   auto go = [&](auto kern) -> cudaError_t {
     // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.
     cudaFuncAttributes fa_attr;
@@ -575,7 +593,7 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
     if (fa_attr.numRegs * kFwdThreads < 2 * 128 * kRegsSoftmax + 128 * kRegsCtl) return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a, pingpong);
+    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a, pingpong, tpc);
     return cudaGetLastError();
   };
 #define FA_FWD_CASE(DD, SKK) \

@@ -18,6 +18,7 @@ FA_MASK_CAUSAL, FA_MASK_WINDOW, FA_MASK_DOCUMENT, FA_MASK_TILE_TABLE, FA_MASK_DO
 FA_SCORE_ALIBI, FA_SCORE_SOFTCAP, FA_SCORE_REL_BIAS = 1, 2, 4
 FA_BLOCK_MASK_EXACT, FA_BLOCK_MASK_REF9 = 0, 1
 FA_NOALLOC_SCRATCH_BYTES = 64 << 20  # static scratch of fa_bwd_noalloc
+FA_TILE_Q2, FA_TILE_Q1, FA_TILE_SOFTMAX_CONCURRENT, FA_TILE_SOFTMAX_TURNS = 1, 2, 4, 8
 
 _i32p = C.POINTER(C.c_int32)
 
@@ -101,6 +102,7 @@ class FaFwdParams(C.Structure):
         ("kernel", C.c_int32),
         ("num_stages", C.c_int32),
         ("status", C.c_void_p),
+        ("tile_cfg", C.c_int32),
     ]
 
 
@@ -129,6 +131,7 @@ class FaBwdParams(C.Structure):
         ("kernel", C.c_int32),
         ("num_stages", C.c_int32),
         ("status", C.c_void_p),
+        ("tile_cfg", C.c_int32),
     ]
 
 

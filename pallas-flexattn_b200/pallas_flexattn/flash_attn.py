@@ -4,7 +4,9 @@ Reference: src/pallas_flexattn/flash_attn.py.  Same entry points and argument
 meaning:
 
 * ``flash_attention(q, k, v, mask_mod=None, block_r=64, block_c=64,
-  num_warps=4, num_stages=3, interpret=False)`` -> o, differentiable
+  num_warps=4, num_stages=None, interpret=False)`` -> o, differentiable
+  (the reference's default num_stages=3 is a Pallas pipelining knob; here None
+  means "the measured choice", see below)
   (``torch.autograd``; the reference uses ``jax.custom_vjp`` with residuals
   ``(q, k, v, o, lse)``, flash_attn.py:464-504);
 * ``flash_attention_fwd(...)`` -> ``(o, lse)`` (flash_attn.py:111-165);
@@ -23,7 +25,10 @@ Rows with no unmasked key give o = 0 and lse = -inf (the reference gives NaN).
 Kernel choice: bf16 with D in {64, 128} runs the tcgen05 kernels on 128x128
 tiles (the MMA-native tile; ``block_r``/``block_c`` are then not used); other
 dtypes and head dims run the generic CUDA-core kernels on ``block_r x block_c``
-tiles.  ``num_stages`` sets the K/V pipeline depth of the tcgen05 forward.
+tiles.  ``num_stages`` sets the pipeline depth of the tcgen05 kernels (K/V
+entries in flight in the forward, Q/dO tiles in the backward); left at None, the
+measured autotuner's cached choice for the problem is used when there is one
+(``kernel_tuner.autotune``), else the kernels' defaults.
 ``num_warps`` and ``interpret`` are accepted for signature compatibility; there
 is no interpreter and no CPU path.
 """
@@ -164,7 +169,22 @@ class _Plan:
         # AUTO lets the library take the tcgen05 kernel of each pass when it applies.
         self.tc = tc
         self.kernel = L.FA_KERNEL_AUTO if tc else L.FA_KERNEL_SIMT
+        # Launch configuration: an explicit num_stages sets the pipeline depth of both passes;
+        # without one, the measured autotuner's entry for this problem (if any) supplies the
+        # depth of each pass and the forward's launch shape, else the kernels' defaults.
         self.num_stages = int(num_stages) if num_stages else 0
+        self.fwd_stages = self.bwd_stages = self.num_stages
+        self.fwd_tile_cfg = 0
+        self.tuned = None
+        if num_stages is None and tc:
+            from .kernel_tuner import make_key, lookup_key, _device_name
+
+            self.tuned = lookup_key(make_key(_device_name(self.device.index or 0), str(q.dtype), q.shape, k.shape,
+                                             mspec, sspec))
+            if self.tuned is not None:
+                self.fwd_stages = int(self.tuned["fwd"]["num_stages"])
+                self.fwd_tile_cfg = int(self.tuned["fwd"]["tile_cfg"])
+                self.bwd_stages = int(self.tuned["bwd"]["num_stages"])
         self.c_mask = mspec.to_c(self.device, Tq, Tkv, *offsets)
         self.c_score = sspec.to_c(self.device, H, Tq, Tkv)
         self.c_tables = bt.to_c()
@@ -179,6 +199,7 @@ class _Plan:
         p.blocks = self.c_tables
         p.kernel = self.kernel
         p.num_stages = self.num_stages
+        p.tile_cfg = 0
         p.status = self.status.data_ptr()
 
 
@@ -187,6 +208,7 @@ def _run_fwd(plan: _Plan, q, k, v) -> Tuple[torch.Tensor, torch.Tensor]:
     lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
     p = L.FaFwdParams()
     plan._fill(p)
+    p.num_stages, p.tile_cfg = plan.fwd_stages, plan.fwd_tile_cfg
     p.q, p.k, p.v, p.o = _fa_tensor(q), _fa_tensor(k), _fa_tensor(v), _fa_tensor(o)
     p.lse = lse.data_ptr()
     with torch.cuda.device(q.device):
@@ -203,6 +225,7 @@ def _run_bwd(plan: _Plan, q, k, v, o, lse, do) -> Tuple[torch.Tensor, torch.Tens
     lse = lse.to(torch.float32).contiguous()
     p = L.FaBwdParams()
     plan._fill(p)
+    p.num_stages = plan.bwd_stages
     p.q, p.k, p.v, p.o, p.dout = _fa_tensor(q), _fa_tensor(k), _fa_tensor(v), _fa_tensor(o), _fa_tensor(do)
     p.dq, p.dk, p.dv = _fa_tensor(dq), _fa_tensor(dk), _fa_tensor(dv)
     p.lse = lse.data_ptr()
@@ -217,7 +240,7 @@ def _run_bwd(plan: _Plan, q, k, v, o, lse, do) -> Tuple[torch.Tensor, torch.Tens
 
 def flash_attention_fwd(q, k, v, mask_mod: Optional[MaskMod] = None, block_r: int = DEFAULT_BLOCK_R,
                         block_c: int = DEFAULT_BLOCK_C, num_warps: int = DEFAULT_NUM_WARPS,
-                        num_stages: int = DEFAULT_NUM_STAGES, interpret: bool = False, *,
+                        num_stages: Optional[int] = None, interpret: bool = False, *,
                         score_mod: Optional[ScoreMod] = None, block_mask: Optional[BlockMask] = None,
                         scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Flash attention forward pass: returns (o, lse)."""
@@ -229,7 +252,7 @@ def flash_attention_fwd(q, k, v, mask_mod: Optional[MaskMod] = None, block_r: in
 
 def flash_attention_bwd(q, k, v, o, logsumexp, do, mask_mod: Optional[MaskMod] = None,
                         block_r: int = DEFAULT_BLOCK_R, block_c: int = DEFAULT_BLOCK_C,
-                        num_warps: int = DEFAULT_NUM_WARPS, num_stages: int = DEFAULT_NUM_STAGES,
+                        num_warps: int = DEFAULT_NUM_WARPS, num_stages: Optional[int] = None,
                         interpret: bool = False, *, score_mod: Optional[ScoreMod] = None,
                         block_mask: Optional[BlockMask] = None,
                         scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -260,7 +283,7 @@ class _FlashAttentionFn(torch.autograd.Function):
 
 def flash_attention(q, k, v, mask_mod: Optional[MaskMod] = None, block_r: int = DEFAULT_BLOCK_R,
                     block_c: int = DEFAULT_BLOCK_C, num_warps: int = DEFAULT_NUM_WARPS,
-                    num_stages: int = DEFAULT_NUM_STAGES, interpret: bool = False, *,
+                    num_stages: Optional[int] = None, interpret: bool = False, *,
                     score_mod: Optional[ScoreMod] = None, block_mask: Optional[BlockMask] = None,
                     scale: Optional[float] = None) -> torch.Tensor:
     """Flash attention with a custom backward pass; returns o."""

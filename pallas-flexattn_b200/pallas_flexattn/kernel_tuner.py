@@ -7,9 +7,12 @@ num_warps, num_stages).  On this engine the table's ``block_r``/``block_c``
 size the tiles of the generic kernels; the tcgen05 kernels always use 128x128.
 
 ``autotune`` replaces the reference's static choice with measurement: it times
-each candidate K/V pipeline depth of the tcgen05 forward with CUDA events on the
-caller's inputs, keeps the fastest, and caches it in memory and in a JSON file
-keyed by (GPU name, dtype, B, H, Tq, Tkv, D, mask key, score flags).
+the launch configurations of the tcgen05 forward (K/V pipeline depth, one or two
+128-row Q tiles per CTA, softmax schedule) and backward (Q/dO pipeline depth)
+with CUDA events on the caller's inputs, keeps the fastest of each pass, and
+caches them in memory and in a JSON file keyed by (GPU name, dtype, B, H, Tq,
+H_kv, Tkv, D, mask flags, score flags).  The attention entry points consult that
+cache whenever ``num_stages`` is not given.
 """
 from __future__ import annotations
 
@@ -85,74 +88,148 @@ def print_kernel_config(batch_size: int, num_heads: int, seq_len: int, head_dim:
 
 # ---------------------------------------------------------------------------- measured autotuning
 _CACHE: Dict[str, dict] = {}
-CACHE_PATH = Path(os.environ.get("FLEXATTN_TUNE_CACHE", Path.home() / ".cache" / "flexattn_b200_tune.json"))
+_LOADED_FROM: Optional[Path] = None
+
+
+def cache_path() -> Path:
+    """JSON file of tuned configurations ($FLEXATTN_TUNE_CACHE, else ~/.cache/flexattn_b200_tune.json)."""
+    return Path(os.environ.get("FLEXATTN_TUNE_CACHE", Path.home() / ".cache" / "flexattn_b200_tune.json"))
 
 
 def _load_cache() -> None:
-    if not _CACHE and CACHE_PATH.exists():
+    global _LOADED_FROM
+    path = cache_path()
+    if _LOADED_FROM == path:
+        return
+    _CACHE.clear()
+    _LOADED_FROM = path
+    if path.exists():
         try:
-            _CACHE.update(json.loads(CACHE_PATH.read_text()))
+            _CACHE.update(json.loads(path.read_text()))
         except (OSError, ValueError):
             pass
 
 
 def _save_cache() -> None:
+    path = cache_path()
     try:
-        CACHE_PATH.parent.mkdir(parents=True, exist_ok=True)
-        CACHE_PATH.write_text(json.dumps(_CACHE, indent=1, sort_keys=True))
+        path.parent.mkdir(parents=True, exist_ok=True)
+        path.write_text(json.dumps(_CACHE, indent=1, sort_keys=True))
     except OSError:
         pass
 
 
-def tune_key(q, k, mask_mod=None, score_mod=None) -> str:
+def clear_memory_cache() -> None:
+    """Forget the in-memory copy; the next lookup reads the cache file again."""
+    global _LOADED_FROM
+    _CACHE.clear()
+    _LOADED_FROM = None
+
+
+@functools.lru_cache(maxsize=16)
+def _device_name(index: int) -> str:
     import torch
 
+    return torch.cuda.get_device_name(index)
+
+
+def make_key(device_name: str, dtype: str, q_shape, k_shape, mask_spec, score_spec) -> str:
+    """Cache key: GPU name, dtype, (B, H, Tq, D), (H_kv, Tkv), mask flags and window, score flags."""
+    mk = None if mask_spec is None else [mask_spec.flags, mask_spec.window_left, mask_spec.window_right]
+    sk = None if score_spec is None else score_spec.flags
+    return json.dumps([device_name, dtype, *map(int, q_shape), int(k_shape[1]), int(k_shape[2]), mk, sk])
+
+
+def tune_key(q, k, mask_mod=None, score_mod=None) -> str:
     from .mask_mod import spec_of as mspec
     from .score_mod import spec_of as sspec
 
-    ms, ss = mspec(mask_mod), sspec(score_mod)
-    mk = None if ms is None else (ms.flags, ms.window_left, ms.window_right)
-    sk = None if ss is None else ss.flags
-    name = torch.cuda.get_device_name(q.device)
-    return json.dumps([name, str(q.dtype), *q.shape, k.shape[1], k.shape[2], mk, sk])
+    return make_key(_device_name(q.device.index or 0), str(q.dtype), q.shape, k.shape, mspec(mask_mod),
+                    sspec(score_mod))
 
 
 def lookup(q, k, mask_mod=None, score_mod=None) -> Optional[dict]:
+    """The tuned entry for this problem, or None."""
     _load_cache()
     return _CACHE.get(tune_key(q, k, mask_mod, score_mod))
 
 
-def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None,
-             stages: Sequence[int] = (2, 3, 4), iters: int = 10, persist: bool = True) -> dict:
-    """Time each candidate pipeline depth of the forward and cache the fastest.
+def lookup_key(key: str) -> Optional[dict]:
+    _load_cache()
+    return _CACHE.get(key)
 
-    Returns ``{"num_stages": n, "ms": t, "candidates": {n: ms, ...}}``.
+
+def _time(fn, iters: int) -> float:
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
+             fwd_stages: Sequence[int] = (0, 2, 3, 4), bwd_stages: Sequence[int] = (2, 3, 4),
+             iters: int = 10, persist: bool = True) -> dict:
+    """Measure the launch configurations of both passes on the caller's inputs and cache the
+    fastest of each (replacing the reference's static choice, kernel_tuner.py:11-65).
+
+    Forward candidates: K/V pipeline depth (``fwd_stages``, entries in flight; 0 = as deep as
+    shared memory holds) x Q tiles per CTA (two 128-row tiles sharing each K/V load, or one)
+    x softmax schedule (concurrent warpgroups, or strict turns when there is no score_mod).
+    Backward candidates: Q/dO pipeline depth (``bwd_stages``).  Each is timed with CUDA events
+    over ``iters`` calls; depths the kernel cannot fit are skipped.  The entry is keyed by
+    (GPU, dtype, shapes, mask flags and window, score flags); ``flash_attention`` and friends
+    use it whenever the caller does not pass ``num_stages``.
+
+    Returns ``{"fwd": {"num_stages", "tile_cfg", "ms"}, "bwd": {"num_stages", "ms"},
+    "candidates": {...}}``.
     """
     import torch
 
-    from .flash_attn import flash_attention_fwd
+    from . import _lib as L
+    from .flash_attn import _Plan, _run_bwd, _run_fwd
 
+    plan = _Plan(q, k, v, mask_mod, score_mod, block_mask, DEFAULT_BLOCK_R, DEFAULT_BLOCK_C, 0, None, need_bwd=True)
+    if not plan.tc:
+        raise ValueError("autotune: only the tcgen05 kernels (bf16, D in {64, 128}) have launch choices")
     key = tune_key(q, k, mask_mod, score_mod)
-    res: Dict[int, float] = {}
-    for ns in stages:
-        def run():
-            flash_attention_fwd(q, k, v, mask_mod, num_stages=ns, score_mod=score_mod, block_mask=block_mask)
+    scheds = [L.FA_TILE_SOFTMAX_CONCURRENT] + ([L.FA_TILE_SOFTMAX_TURNS] if plan.sspec.flags == 0 else [])
+    fwd_res: Dict[str, float] = {}
+    for ns in fwd_stages:
+        for tiles in (L.FA_TILE_Q2, L.FA_TILE_Q1):
+            for sch in (scheds if tiles == L.FA_TILE_Q2 else [L.FA_TILE_SOFTMAX_CONCURRENT]):
+                plan.fwd_stages, plan.fwd_tile_cfg = ns, tiles | sch
+                try:
+                    ms = _time(lambda: _run_fwd(plan, q, k, v), iters)
+                except L.FlexAttnError:
+                    continue
+                fwd_res[json.dumps([ns, tiles | sch])] = ms
+    if not fwd_res:
+        raise RuntimeError("autotune: no forward candidate ran")
+    best_f = json.loads(min(fwd_res, key=fwd_res.get))
+    plan.fwd_stages, plan.fwd_tile_cfg = best_f
+    o, lse = _run_fwd(plan, q, k, v)
+    do = torch.randn_like(o)
+    bwd_res: Dict[str, float] = {}
+    for ns in bwd_stages:
+        plan.bwd_stages = ns
         try:
-            run()
-        except Exception:  # a depth the kernel cannot fit is skipped
+            bwd_res[str(ns)] = _time(lambda: _run_bwd(plan, q, k, v, o, lse, do), iters)
+        except L.FlexAttnError:
             continue
-        torch.cuda.synchronize(q.device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(iters):
-            run()
-        end.record()
-        end.synchronize()
-        res[ns] = start.elapsed_time(end) / iters
-    if not res:
-        raise RuntimeError("autotune: no candidate configuration ran")
-    best = min(res, key=res.get)
-    entry = {"num_stages": best, "ms": res[best], "candidates": {str(k_): v_ for k_, v_ in res.items()}}
+    if not bwd_res:
+        raise RuntimeError("autotune: no backward candidate ran")
+    best_b = int(min(bwd_res, key=bwd_res.get))
+    entry = {"fwd": {"num_stages": best_f[0], "tile_cfg": best_f[1], "ms": fwd_res[json.dumps(best_f)]},
+             "bwd": {"num_stages": best_b, "ms": bwd_res[str(best_b)]},
+             "candidates": {"fwd [num_stages, tile_cfg]": fwd_res, "bwd num_stages": bwd_res}}
+    _load_cache()
     _CACHE[key] = entry
     if persist:
         _save_cache()

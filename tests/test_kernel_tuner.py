@@ -56,3 +56,28 @@ def test_print_kernel_config(capsys):
     out = capsys.readouterr().out
     assert "BLOCK_R (block_r):      128" not in out or "NUM_WARPS" in out
     assert "block_r=64" in out and "num_stages=3" in out
+
+
+def test_tuned_cache_round_trip(tmp_path, monkeypatch):
+    """The measured tuner's cache: entries persist to the JSON file and are read back by key
+    (the planner's lookup) after the in-memory copy is dropped.  No GPU needed."""
+    from pallas_flexattn import kernel_tuner as KT
+    from pallas_flexattn.mask_mod import spec_of as mspec
+    from pallas_flexattn.score_mod import spec_of as sspec
+    import pallas_flexattn as pf
+
+    monkeypatch.setenv("FLEXATTN_TUNE_CACHE", str(tmp_path / "tune.json"))
+    KT.clear_memory_cache()
+    key = KT.make_key("NVIDIA B200", "torch.bfloat16", (1, 4, 1024, 128), (1, 4, 1024, 128),
+                      mspec(pf.causal_mask), sspec(None))
+    other = KT.make_key("NVIDIA B200", "torch.bfloat16", (1, 4, 1024, 128), (1, 4, 1024, 128),
+                        mspec(pf.sliding_window_mask(64, 0)), sspec(None))
+    assert key != other
+    assert KT.lookup_key(key) is None
+    entry = {"fwd": {"num_stages": 2, "tile_cfg": 5, "ms": 0.1}, "bwd": {"num_stages": 3, "ms": 0.2}}
+    KT._CACHE[key] = entry
+    KT._save_cache()
+    KT.clear_memory_cache()
+    assert KT.lookup_key(key) == entry and KT.lookup_key(other) is None
+    monkeypatch.setenv("FLEXATTN_TUNE_CACHE", str(tmp_path / "elsewhere.json"))
+    assert KT.lookup_key(key) is None  # a different cache file is a different cache
