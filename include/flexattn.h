@@ -63,6 +63,11 @@ enum {
  *                                                         (mask_mod.py:25-43)
  *   DOCUMENT    doc_q[b][q] == doc_kv[b][kv]              (mask_mod.py:46-59 stub, built here)
  *   TILE_TABLE  table[q / table_block][kv / table_block] != 0
+ *   BITMASK     an arbitrary predicate evaluated beforehand into 128 x 128 tiles (the
+ *               Python mask_mod callables outside the registry): bit_index[lq/128][lk/128]
+ *               is -1 (tile fully masked), -2 (fully allowed) or a slot s whose bits
+ *               bits[s][lq%128][(lk%128)/32] >> (lk%32) & 1 hold the predicate, with lq, lk
+ *               the LOCAL positions (q - q_offset, kv - kv_offset)
  * No flag set = bidirectional (mask_mod.py:20-22).  Elements with kv >= Tkv are
  * always masked.  Predicates (and the position-dependent score mods) see global
  * positions q + q_offset and kv + kv_offset, so a caller can run one block of a
@@ -72,7 +77,8 @@ enum { FA_MASK_CAUSAL = 1, FA_MASK_WINDOW = 2, FA_MASK_DOCUMENT = 4, FA_MASK_TIL
        /* with FA_MASK_DOCUMENT: the ids are non-decreasing along the sequence (contiguous
           documents), so the tcgen05 kernels reduce "same document" to one position interval
           per row instead of testing it per element */
-       FA_MASK_DOC_SORTED = 16 };
+       FA_MASK_DOC_SORTED = 16,
+       FA_MASK_BITMASK = 32 };
 
 typedef struct {
   int32_t flags;
@@ -83,6 +89,9 @@ typedef struct {
   const uint8_t* tile_table;         /* [table_rows, table_cols] device bytes, nonzero = keep */
   int32_t table_rows, table_cols, table_block;
   int32_t q_offset, kv_offset;       /* global position of row 0 of q / of k, v */
+  const int32_t* bit_index;          /* BITMASK: [bit_rows, bit_cols] device int32 */
+  const uint32_t* bits;              /* BITMASK: [slots, 128, 4] device words */
+  int32_t bit_rows, bit_cols;        /* ceil(Tq / 128), ceil(Tkv / 128) */
 } FaMaskSpec;
 
 /* ------------------------------------------------------------------ score_mod registry

@@ -112,8 +112,12 @@ int check_common(int dtype, int B, int H, int Hkv, int Tq, int Tkv, int D, const
     return fail(FA_ERR_INVALID, "document mask without document ids");
   if ((m.flags & FA_MASK_TILE_TABLE) && (!m.tile_table || m.table_block <= 0 || m.table_cols <= 0))
     return fail(FA_ERR_INVALID, "tile-table mask without a table");
-  if (m.flags & ~(FA_MASK_CAUSAL | FA_MASK_WINDOW | FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE | FA_MASK_DOC_SORTED))
+  if (m.flags & ~(FA_MASK_CAUSAL | FA_MASK_WINDOW | FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE | FA_MASK_DOC_SORTED |
+                  FA_MASK_BITMASK))
     return fail(FA_ERR_INVALID, "unknown mask flags 0x%x", m.flags);
+  if ((m.flags & FA_MASK_BITMASK) &&
+      (!m.bit_index || !m.bits || m.bit_rows < (Tq + 127) / 128 || m.bit_cols < (Tkv + 127) / 128))
+    return fail(FA_ERR_INVALID, "bitmask mask without tables covering %d x %d positions", Tq, Tkv);
   if ((m.flags & FA_MASK_DOC_SORTED) && !(m.flags & FA_MASK_DOCUMENT))
     return fail(FA_ERR_INVALID, "FA_MASK_DOC_SORTED needs FA_MASK_DOCUMENT");
   if (s.flags & ~(FA_SCORE_ALIBI | FA_SCORE_SOFTCAP | FA_SCORE_REL_BIAS))
@@ -330,6 +334,9 @@ int fa_create_block_mask(const FaMaskSpec* mask, int32_t B, int32_t Tq, int32_t 
     return fail(FA_ERR_INVALID, "document mask without document ids");
   if ((mask->flags & FA_MASK_TILE_TABLE) && (!mask->tile_table || mask->table_block <= 0))
     return fail(FA_ERR_INVALID, "tile-table mask without a table");
+  if ((mask->flags & FA_MASK_BITMASK) && (!mask->bit_index || !mask->bits || mask->bit_rows < (Tq + 127) / 128 ||
+                                          mask->bit_cols < (Tkv + 127) / 128))
+    return fail(FA_ERR_INVALID, "bitmask mask without tables covering %d x %d positions", Tq, Tkv);
   if (!out->tile_class || !out->kv_num_blocks || !out->kv_indices || !out->full_kv_num_blocks ||
       !out->full_kv_indices || !out->q_num_blocks || !out->q_indices || !out->full_q_num_blocks || !out->full_q_indices)
     return fail(FA_ERR_INVALID, "an output table pointer is NULL");

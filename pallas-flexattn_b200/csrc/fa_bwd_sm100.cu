@@ -472,7 +472,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       q_lo = max(q_lo, f);
       q_hi = min(q_hi, l);
     }
-    const bool per_elem_mask = (mc.flags & FA_MASK_TILE_TABLE) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
+    const bool per_elem_mask =
+        (mc.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];

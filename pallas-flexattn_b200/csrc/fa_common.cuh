@@ -98,6 +98,9 @@ struct MaskCtx {
   const int32_t* doc_kv;
   const uint8_t* table;
   int table_cols, table_block;
+  const int32_t* bit_index;  // BITMASK tiles (local positions)
+  const uint32_t* bits;
+  int bit_rows, bit_cols;
 };
 
 __device__ inline MaskCtx make_mask_ctx(const FaMaskSpec& m, int b, int Tkv) {
@@ -113,6 +116,10 @@ __device__ inline MaskCtx make_mask_ctx(const FaMaskSpec& m, int b, int Tkv) {
   c.table = m.tile_table;
   c.table_cols = m.table_cols;
   c.table_block = m.table_block > 0 ? m.table_block : 1;
+  c.bit_index = m.bit_index;
+  c.bits = m.bits;
+  c.bit_rows = m.bit_rows;
+  c.bit_cols = m.bit_cols;
   return c;
 }
 
@@ -129,6 +136,17 @@ __device__ __forceinline__ bool mask_ok(const MaskCtx& m, int q, int kv, int dq)
   if (m.flags & FA_MASK_DOCUMENT) ok = ok && (kv < m.Tkv) && (__ldg(m.doc_kv + kv) == dq);
   if (m.flags & FA_MASK_TILE_TABLE)
     ok = ok && (m.table[(q / m.table_block) * m.table_cols + kv / m.table_block] != 0);
+  if ((m.flags & FA_MASK_BITMASK) && ok) {
+    const int lq = q - m.q_off, lk = kv - m.kv_off;  // local positions
+    if ((unsigned)(lq >> 7) >= (unsigned)m.bit_rows || (unsigned)(lk >> 7) >= (unsigned)m.bit_cols) {
+      ok = false;
+    } else {
+      const int slot = __ldg(m.bit_index + (lq >> 7) * m.bit_cols + (lk >> 7));
+      if (slot == -1) ok = false;
+      else if (slot >= 0)
+        ok = (__ldg(m.bits + ((int64_t)slot * 128 + (lq & 127)) * 4 + ((lk & 127) >> 5)) >> (lk & 31)) & 1u;
+    }
+  }
   return ok;
 }
 

@@ -358,7 +358,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       row_lo = max(row_lo, f);
       row_hi = min(row_hi, l);
     }
-    const bool per_elem_mask = (mc.flags & FA_MASK_TILE_TABLE) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
+    const bool per_elem_mask =
+        (mc.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
 
     // Turn-taking is compiled only where the host may enable it (no score_mod).
     constexpr bool PP = SK == SC_NONE;
@@ -576,7 +577,7 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   // warpgroups in flight at once.  tile_cfg bits 2-3 override the choice; with one Q tile
   // per CTA there is no second warpgroup to take turns with.
 #if FA_FWD_PINGPONG < 0
-  const bool per_elem = (a.mask.flags & FA_MASK_TILE_TABLE) ||
+  const bool per_elem = (a.mask.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) ||
                         ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
   int pingpong = a.D == 128 && sk == SC_NONE && !per_elem;
   if ((tile_cfg & 12) == FA_TILE_SOFTMAX_CONCURRENT) pingpong = 0;

@@ -15,6 +15,7 @@ FA_OK, FA_ERR_INVALID, FA_ERR_UNSUPPORTED, FA_ERR_CUDA, FA_ERR_TIMEOUT = 0, 1, 2
 FA_DTYPE_F32, FA_DTYPE_BF16 = 0, 1
 FA_KERNEL_AUTO, FA_KERNEL_TC, FA_KERNEL_SIMT = 0, 1, 2
 FA_MASK_CAUSAL, FA_MASK_WINDOW, FA_MASK_DOCUMENT, FA_MASK_TILE_TABLE, FA_MASK_DOC_SORTED = 1, 2, 4, 8, 16
+FA_MASK_BITMASK = 32
 FA_SCORE_ALIBI, FA_SCORE_SOFTCAP, FA_SCORE_REL_BIAS = 1, 2, 4
 FA_BLOCK_MASK_EXACT, FA_BLOCK_MASK_REF9 = 0, 1
 FA_NOALLOC_SCRATCH_BYTES = 64 << 20  # static scratch of fa_bwd_noalloc
@@ -37,6 +38,10 @@ class FaMaskSpec(C.Structure):
         ("table_block", C.c_int32),
         ("q_offset", C.c_int32),
         ("kv_offset", C.c_int32),
+        ("bit_index", C.c_void_p),
+        ("bits", C.c_void_p),
+        ("bit_rows", C.c_int32),
+        ("bit_cols", C.c_int32),
     ]
 
 

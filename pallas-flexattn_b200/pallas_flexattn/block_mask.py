@@ -18,11 +18,10 @@ import math
 from dataclasses import dataclass, field
 from typing import Optional
 
-import numpy as np
 import torch
 
 from . import _lib as L
-from .mask_mod import MaskMod, MaskSpec, spec_of
+from .mask_mod import MaskMod, MaskSpec, evaluate_mask, spec_of
 
 
 @dataclass(frozen=True, eq=False)
@@ -184,54 +183,26 @@ class BlockMask:
         return self._dev[k]
 
 
-def _ref9_host(mask_mod: MaskMod, Q_LEN: int, KV_LEN: int, block_size: int) -> np.ndarray:
-    """The reference 3x3 sampling rule, vectorised over all tiles (for callables outside the registry)."""
-    nq, nkv = math.ceil(Q_LEN / block_size), math.ceil(KV_LEN / block_size)
-    qs = np.arange(nq) * block_size
-    qe = np.minimum(qs + block_size, Q_LEN)
-    ks = np.arange(nkv) * block_size
-    ke = np.minimum(ks + block_size, KV_LEN)
-    qsamp = np.stack([qs, (qs + qe) // 2, qe - 1], axis=1)  # [nq, 3]
-    ksamp = np.stack([ks, (ks + ke) // 2, ke - 1], axis=1)  # [nkv, 3]
-    qi = torch.as_tensor(qsamp[:, :, None, None])
-    ki = torch.as_tensor(ksamp[None, None, :, :])
-    m = mask_mod(qi, ki)
-    m = torch.as_tensor(np.asarray(m)) if not isinstance(m, torch.Tensor) else m
-    m = torch.broadcast_to(m, (nq, 3, nkv, 3))
-    return m.any(dim=3).any(dim=1).cpu().numpy()
-
-
-def _lists_from_dense(valid: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
-    counts = valid.sum(axis=1).astype(np.int32)
-    max_row = int(counts.max()) if counts.size else 0
-    cols = np.full((valid.shape[0], max_row), -1, dtype=np.int32)
-    for i in range(valid.shape[0]):
-        idx = np.nonzero(valid[i])[0]
-        cols[i, : idx.size] = idx
-    return counts, cols
-
-
 def create_block_mask(mask_mod: MaskMod, B: int, H: int, Q_LEN: int, KV_LEN: int, block_size: int = 128, *,
                       device=None) -> BlockMask:
     """Create a BlockMask from a mask_mod (reference block_mask.py:54-129).
 
     ``num_blocks_in_row`` / ``col_indices`` follow the reference's 3x3 sampling
-    rule exactly.  ``tables`` hold the exact classification (a tile is listed iff
+    rule exactly, for registry masks and arbitrary callables alike (a callable is
+    first evaluated on the GPU into per-tile bitmasks, which the classifier reads).  ``tables`` hold the exact classification (a tile is listed iff
     any element is unmasked, and marked full iff all are), which the attention
     kernels use.  B and H do not change the result, as in the reference; a
     document mask with per-batch ids yields per-batch tables and batch 0's
     reference fields.
     """
     del H
-    spec = spec_of(mask_mod)
-    if spec is None:
-        valid = _ref9_host(mask_mod, Q_LEN, KV_LEN, block_size)
-        counts, cols = _lists_from_dense(valid)
-        return BlockMask(torch.from_numpy(counts), torch.from_numpy(cols), block_size, Q_LEN, KV_LEN, None, mask_mod)
     if device is None:
         if not torch.cuda.is_available():
             raise RuntimeError("create_block_mask runs on the GPU; no CUDA device is available")
         device = torch.device("cuda", torch.cuda.current_device())
+    spec = spec_of(mask_mod)
+    if spec is None:  # an arbitrary callable: evaluated on the GPU into per-tile bitmasks first
+        spec = evaluate_mask(mask_mod, Q_LEN, KV_LEN, device)
     ref = build_tables_from_spec(spec, B, Q_LEN, KV_LEN, block_size, block_size, device, L.FA_BLOCK_MASK_REF9)
     exact = build_tables_from_spec(spec, B, Q_LEN, KV_LEN, block_size, block_size, device, L.FA_BLOCK_MASK_EXACT)
     counts = ref.kv_num_blocks[0].contiguous()

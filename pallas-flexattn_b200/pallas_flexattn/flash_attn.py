@@ -43,7 +43,7 @@ import torch
 
 from . import _lib as L
 from .block_mask import BlockMask, BlockTables, build_tables_from_spec
-from .mask_mod import MaskMod, MaskSpec
+from .mask_mod import MaskMod, MaskSpec, evaluate_mask
 from .mask_mod import spec_of as mask_spec_of
 from .score_mod import ScoreMod, ScoreSpec
 from .score_mod import spec_of as score_spec_of
@@ -143,9 +143,8 @@ class _Plan:
             mask_mod = block_mask.mask_mod
         mspec = mask_spec_of(mask_mod)
         if mspec is None:
-            raise NotImplementedError(
-                "this mask_mod has no registry entry; build it from causal_mask, sliding_window_mask, "
-                "document_mask, tile_mask or and_masks")
+            # an arbitrary callable: evaluated once per geometry on the GPU into per-tile bitmasks
+            mspec = evaluate_mask(mask_mod, Tq, Tkv, self.device, *offsets)
         sspec = score_spec_of(score_mod)
         if sspec is None:
             raise NotImplementedError(

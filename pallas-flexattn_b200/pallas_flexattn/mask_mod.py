@@ -37,6 +37,8 @@ class MaskSpec:
     doc_sorted: bool = False                   # ids non-decreasing along T (contiguous documents)
     tile_table: Optional[torch.Tensor] = None  # [rows, cols] uint8, nonzero = keep
     table_block: int = 0
+    bit_index: Optional[torch.Tensor] = None   # BITMASK: [ceil(Tq/128), ceil(Tkv/128)] int32 (device)
+    bits: Optional[torch.Tensor] = None        # BITMASK: [slots, 128, 4] int32 words (device)
     _dev: dict = field(default_factory=dict, repr=False, compare=False)
 
     def key(self) -> tuple:
@@ -47,6 +49,7 @@ class MaskSpec:
             None if self.doc_ids is None else id(self.doc_ids),
             None if self.tile_table is None else id(self.tile_table),
             self.table_block,
+            None if self.bits is None else id(self.bits),
         )
 
     @property
@@ -88,7 +91,73 @@ class MaskSpec:
             m.tile_table = t.data_ptr()
             m.table_rows, m.table_cols = t.shape
             m.table_block = self.table_block
+        if self.flags & L.FA_MASK_BITMASK:
+            if self.bit_index.device != device:
+                raise ValueError("a mask_mod evaluated on one device cannot run on another")
+            m.bit_index, m.bits = self.bit_index.data_ptr(), self.bits.data_ptr()
+            m.bit_rows, m.bit_cols = self.bit_index.shape
         return m
+
+
+BIT_TILE = 128  # tile edge of the evaluated bitmask of an arbitrary mask_mod
+_CALLABLE_SPECS: dict = {}
+_CALLABLE_SPECS_MAX = 32
+
+
+def _pack_bits(tiles: torch.Tensor) -> torch.Tensor:
+    """[n, 128, 128] bool -> [n, 128, 4] int32 words (bit j of word w = column 32 w + j)."""
+    n = tiles.shape[0]
+    w = tiles.reshape(n, BIT_TILE, 4, 32).to(torch.int64)
+    words = (w << torch.arange(32, device=tiles.device, dtype=torch.int64)).sum(-1)
+    return (words - ((words >> 31) << 32)).to(torch.int32)  # two's complement view of the uint32
+
+
+def evaluate_mask(mask_mod: MaskMod, Tq: int, Tkv: int, device, q_offset: int = 0, kv_offset: int = 0,
+                  rows_per_chunk: int = 1024) -> MaskSpec:
+    """Evaluate an arbitrary mask_mod (a callable of index tensors, no registry entry) on the
+    GPU over the whole (Tq, Tkv) grid at global positions (q + q_offset, kv + kv_offset),
+    in chunks of rows, into 128 x 128 tiles: each tile is classified fully masked, fully
+    allowed or mixed, and mixed tiles keep their predicate as 128 x 128 bits.  The result is
+    a BITMASK spec the kernels (and the block-table builder) test per element.  Cached per
+    (callable, geometry, device) while the callable is alive."""
+    device = torch.device(device)
+    key = (id(mask_mod), Tq, Tkv, q_offset, kv_offset, str(device))
+    hit = _CALLABLE_SPECS.get(key)
+    if hit is not None and hit[0] is mask_mod:
+        return hit[1]
+    nbq, nbk = -(-Tq // BIT_TILE), -(-Tkv // BIT_TILE)
+    index = torch.empty((nbq, nbk), dtype=torch.int32, device=device)
+    slots = []
+    n_slots = 0
+    ki = torch.arange(nbk * BIT_TILE, device=device)
+    kvalid = ki < Tkv
+    step = max(BIT_TILE, rows_per_chunk // BIT_TILE * BIT_TILE)
+    for r0 in range(0, nbq * BIT_TILE, step):
+        r1 = min(r0 + step, nbq * BIT_TILE)
+        qi = torch.arange(r0, r1, device=device)
+        m = mask_mod((qi + q_offset)[:, None], (ki + kv_offset)[None, :])
+        m = torch.as_tensor(m, device=device)
+        m = torch.broadcast_to(m, (r1 - r0, nbk * BIT_TILE)).to(torch.bool)
+        valid = (qi < Tq)[:, None] & kvalid[None, :]
+        allowed = m & valid
+        nr = (r1 - r0) // BIT_TILE
+        tiles = allowed.reshape(nr, BIT_TILE, nbk, BIT_TILE).permute(0, 2, 1, 3)  # [nr, nbk, 128, 128]
+        any_ = tiles.any(dim=(2, 3))
+        all_ = (m | ~valid).reshape(nr, BIT_TILE, nbk, BIT_TILE).all(dim=3).all(dim=1)  # padding counts as allowed
+        cls = torch.where(any_ & all_, -2, -1).to(torch.int32)
+        mixed = any_ & ~all_
+        nm = int(mixed.sum())
+        if nm:
+            cls[mixed] = torch.arange(n_slots, n_slots + nm, device=device, dtype=torch.int32)
+            slots.append(_pack_bits(tiles[mixed]))
+            n_slots += nm
+        index[r0 // BIT_TILE:r1 // BIT_TILE] = cls
+    bits = torch.cat(slots) if slots else torch.zeros((1, BIT_TILE, 4), dtype=torch.int32, device=device)
+    spec = MaskSpec(flags=L.FA_MASK_BITMASK, bit_index=index.contiguous(), bits=bits.contiguous())
+    _CALLABLE_SPECS[key] = (mask_mod, spec)
+    while len(_CALLABLE_SPECS) > _CALLABLE_SPECS_MAX:
+        _CALLABLE_SPECS.pop(next(iter(_CALLABLE_SPECS)))
+    return spec
 
 
 def spec_of(mask_mod: Optional[MaskMod]) -> Optional[MaskSpec]:

@@ -95,3 +95,24 @@ def test_per_batch_document_tables():
     for b in range(2):
         cls = O.block_mask_exact(O.and_(O.document(d[b].numpy()), O.causal), 256, 256, 128, 128)
         np.testing.assert_array_equal(bm.tables.tile_class[b].cpu().numpy(), cls)
+
+
+def test_create_block_mask_from_a_lambda_is_bit_exact():
+    """An arbitrary callable (no registry entry) is evaluated on the GPU into per-tile bitmasks;
+    the reference fields still follow the 3x3 rule bit for bit and the tables are exact."""
+    band = lambda q, kv: ((q - kv) >= 100) & ((q - kv) <= 110)  # noqa: E731
+    bm = pf.create_block_mask(band, 1, 1, 1024, 1024, 128)
+    np.testing.assert_array_equal(bm.num_blocks_in_row.cpu().numpy(), BM["band100_110_T1024_b128/num"])
+    np.testing.assert_array_equal(bm.col_indices.cpu().numpy(), BM["band100_110_T1024_b128/cols"])
+    cls = O.block_mask_exact(lambda q, kv: ((q - kv) >= 100) & ((q - kv) <= 110), 1024, 1024, 128, 128)
+    np.testing.assert_array_equal(bm.tables.tile_class[0].cpu().numpy(), cls)
+
+
+@pytest.mark.parametrize("T,bs", [(1000, 128), (300, 64), (777, 96)])
+def test_lambda_tables_match_oracle_exact(T, bs):
+    mm = lambda q, kv: ((q * 7 + kv * 3) % 11 < 4) | (q == kv)  # noqa: E731 (scattered pattern)
+    bm = pf.create_block_mask(mm, 1, 1, T, T, bs)
+    cls = O.block_mask_exact(mm, T, T, bs, bs)
+    np.testing.assert_array_equal(bm.tables.tile_class[0].cpu().numpy(), cls)
+    num, cols = O.block_mask_ref9(mm, T, T, bs)
+    np.testing.assert_array_equal(bm.num_blocks_in_row.cpu().numpy(), num)

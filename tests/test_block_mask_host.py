@@ -11,7 +11,6 @@ import pallas_flexattn as pf
 from oracle import flexattn_oracle as O
 from pallas_flexattn import _lib as L
 from pallas_flexattn import workloads as W
-from pallas_flexattn.block_mask import _ref9_host
 from pallas_flexattn.mask_mod import spec_of
 
 BM = np.load(Path(__file__).resolve().parent / "golden" / "block_masks.npz")
@@ -76,13 +75,10 @@ def test_window_builder_golden(T, w, bs):
     np.testing.assert_array_equal(bm.col_indices.numpy(), BM[f"windowbuilder_T{T}_w{w}_b{bs}/cols"])
 
 
-def test_create_block_mask_arbitrary_callable_uses_reference_rule_on_host():
-    band = lambda q, kv: ((q - kv) >= 100) & ((q - kv) <= 110)  # noqa: E731 (no registry entry)
-    bm = pf.create_block_mask(band, 1, 1, 1024, 1024, 128)
-    np.testing.assert_array_equal(bm.num_blocks_in_row.numpy(), BM["band100_110_T1024_b128/num"])
-    valid = _ref9_host(pf.sliding_window_mask(16, 16), 300, 300, 64)
-    num, cols = O.lists_from_valid(valid)
+def test_oracle_reference_rule_on_window_golden():
+    num, cols = O.block_mask_ref9(O.sliding_window(16, 16), 300, 300, 64)
     np.testing.assert_array_equal(num, BM["window16_16_T300_b64/num"])
+    np.testing.assert_array_equal(cols, BM["window16_16_T300_b64/cols"])
 
 
 @pytest.mark.parametrize("mm,om", [

@@ -335,3 +335,31 @@ def test_bwd_preprocess_entry_point(D, T):
     ref = (o.float() * do.float()).sum(-1).flatten()
     torch.testing.assert_close(delta, ref, atol=1e-4, rtol=1e-5)
     assert int((acc != 0).sum()) == 0
+
+
+LAMBDAS = {
+    # a band 100..110 back (no registry entry; fully masked rows at the start)
+    "band": lambda q, kv: ((q - kv) >= 100) & ((q - kv) <= 110),
+    # scattered keys plus the diagonal, causal
+    "scatter": lambda q, kv: (((q * 7 + kv * 3) % 11 < 4) | (q == kv)) & (q >= kv),
+    # prefix-LM: a bidirectional prefix of 200 positions, causal after it
+    "prefix_lm": lambda q, kv: (kv < 200) | (q >= kv),
+}
+
+
+@pytest.mark.parametrize("name", list(LAMBDAS))
+@pytest.mark.parametrize("dtype,D,T", [(torch.bfloat16, 128, 1000), (torch.bfloat16, 64, 640),
+                                       (torch.float32, 64, 300)])
+def test_arbitrary_mask_callable(name, dtype, D, T):
+    """A mask_mod with no registry entry: evaluated on the GPU into per-tile bitmasks and
+    tested per element by the kernels (tcgen05 for bf16, generic for fp32)."""
+    fn = LAMBDAS[name]
+    q, k, v, do = inputs((1, 2, T, D), (1, 2, T, D), dtype, seed=T + D)
+    check_all(q, k, v, do, fn, fn)
+
+
+def test_arbitrary_callable_inside_and_masks_with_score_mod():
+    mm = pf.and_masks(pf.sliding_window_mask(300, 0), lambda q, kv: (kv % 4) != 1)  # callable part -> callable
+    om = O.and_(O.sliding_window(300, 0), lambda q, kv: (kv % 4) != 1)
+    q, k, v, do = inputs((2, 2, 768, 128), (2, 2, 768, 128), torch.bfloat16, seed=5)
+    check_all(q, k, v, do, mm, om, pf.softcap_score_mod(20.0), (O.softcap(20.0),))
