@@ -146,6 +146,8 @@ typedef struct {
 enum {
   FA_TILE_Q2 = 1,                 /* two 128-row Q tiles per CTA sharing each K/V tile load */
   FA_TILE_Q1 = 2,                 /* one Q tile per CTA (twice the CTAs; for small grids) */
+  FA_TILE_HEADS2 = 3,             /* one Q tile of two heads per CTA: both walk the same kv list
+                                     (irregular sparse masks); H must be even */
   FA_TILE_SOFTMAX_CONCURRENT = 4, /* both softmax warpgroups run at once */
   FA_TILE_SOFTMAX_TURNS = 8,      /* strict turns per kv tile (no score_mod only) */
 };

@@ -114,16 +114,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   int* entries = reinterpret_cast<int*>(smem + L.ent_off);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // tpc = Q tiles per CTA: 2 (sub-tiles 0 and 1 are q tiles 2u and 2u+1, sharing every K/V
-  // load) or 1 (q tile u only; sub-tile 1 gets the invalid index nq and idles, which doubles
-  // the CTAs for grids that would not fill the SMs).
+  // Launch shape `tpc`:
+  //   2  sub-tiles 0 and 1 are q tiles 2u and 2u+1 of one head, sharing every K/V load (the
+  //      CTA walks the union of their kv lists);
+  //   1  q tile u only; sub-tile 1 gets the invalid index nq and idles (twice the CTAs, for
+  //      grids that would not fill the SMs);
+  //   3  q tile u of heads 2g and 2g+1: both sub-tiles walk the same kv list (tables do not
+  //      depend on the head), so neither idles when the list is irregular; each entry loads
+  //      K and V of both heads, or once when both heads share a K/V head (grouped queries).
+  const bool hpair = tpc == 3;
+  const int HU = hpair ? a.H / 2 : a.H;  // head units per batch row
   const int nunits = tpc == 2 ? (a.bt.nq + 1) >> 1 : a.bt.nq;
-  const int bh = blockIdx.x % (a.B * a.H);
-  const int unit = nunits - 1 - (int)(blockIdx.x / (a.B * a.H));  // heaviest (last) q rows first
+  const int bhu = blockIdx.x % (a.B * HU);
+  const int unit = nunits - 1 - (int)(blockIdx.x / (a.B * HU));  // heaviest (last) q rows first
+  const int b = bhu / HU;
+  const int h0 = hpair ? 2 * (bhu % HU) : bhu % HU, h1 = hpair ? h0 + 1 : h0;
   const int qt0 = tpc == 2 ? 2 * unit : unit;
-  const int qt1 = tpc == 2 ? 2 * unit + 1 : a.bt.nq;
-  const int b = bh / a.H, h = bh % a.H;
-  const int hk = h / (a.H / a.Hkv);
+  const int qt1 = tpc == 2 ? 2 * unit + 1 : (hpair ? unit : a.bt.nq);
+  const int hk0 = h0 / (a.H / a.Hkv), hk1 = h1 / (a.H / a.Hkv);
+  const bool kv2 = hk1 != hk0;     // two K/V heads: each entry is K0, K1, V0, V1 (else K, V)
+  const int LPE = kv2 ? 4 : 2;     // loads per kv entry
 
   // ---------------------------------------------------------------- setup
   if (warp == 8 && lane == 0) {
@@ -157,11 +167,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // Mark the kv tiles each sub-tile visits: bits 0-1 sub-tile 0, bits 2-3 sub-tile 1;
   // code 1 = partial (mask applied), 2 = full.
   {
-    const int64_t head = table_head(a.bt, b, h);
     for (int i = 0; i < 2; ++i) {
       const int qt = i ? qt1 : qt0;
       if (qt >= a.bt.nq) continue;
-      const int64_t row = head * a.bt.nq + qt;
+      const int64_t row = table_head(a.bt, b, i ? h1 : h0) * a.bt.nq + qt;
       const int np = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[row] : 0;
       for (int e = tid; e < np; e += kFwdThreads) {
         const int j = a.bt.kv_indices[row * a.bt.kv_cap + e];
@@ -208,18 +217,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
       for (int i = 0; i < (has1 ? 2 : 1); ++i)
         for (int c = 0; c < NCHUNK; ++c)
-          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (i ? qt1 : qt0) * kBM, h, b);
+          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (i ? qt1 : qt0) * kBM,
+                      i ? h1 : h0, b);
       bool ok = true;
-      int issued = 0;  // loads issued so far (K and V alternate)
+      int issued = 0;  // loads issued so far: per entry K, V (one K/V head) or K0, K1, V0, V1
       for (int t = 0; t < n_ent && ok; ++t) {
         const int j = entries[t] & 0xFFFFFF;
-        for (int w = 0; w < 2 && ok; ++w, ++issued) {
+        for (int w = 0; w < LPE && ok; ++w, ++issued) {
           const int slot = issued % NS, use = issued / NS;
           if (!mbar_wait(bar_kv_empty + slot, (use & 1) ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(bar_kv_full + slot, L.tile_bytes);
+          const bool is_v = w >= LPE / 2;
+          const int kvh = (kv2 && (w & 1)) ? hk1 : hk0;
           for (int c = 0; c < NCHUNK; ++c)
-            tma_load_4d(sKV + slot * L.tile_bytes + c * CHUNK_BYTES, w ? &tm_v : &tm_k, bar_kv_full + slot, c * 64,
-                        j * kBN, hk, b);
+            tma_load_4d(sKV + slot * L.tile_bytes + c * CHUNK_BYTES, is_v ? &tm_v : &tm_k, bar_kv_full + slot,
+                        c * 64, j * kBN, kvh, b);
         }
       }
       if (!ok) {
@@ -264,50 +276,56 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t v_lo0 = (uint32_t)make_smem_desc(sKVa, CHUNK_BYTES, 1024, SMEM_SWIZZLE_128B);
       const uint32_t s_dst = tmem_base + TM_S0 + 128 * i, o_dst = tmem_base + TM_O0 + D * i;
 
-      // S_i(t) = Q_i K_t^T (if this sub-tile visits entry t), then release K_t's slot.
+      // S_i(t) = Q_i K_t^T (if this sub-tile visits entry t), then release the K slots of entry
+      // t.  Every slot is released by both issuers once per use (empty barriers count two
+      // arrivals), and a release may only follow the load of the same use, so a slot this
+      // sub-tile does not read (the other head's K with two K/V heads, or an entry it skips)
+      // is still awaited before it is released: neither thread can release a slot's next use
+      // before the other has released the current one.
       auto issue_s = [&](int t, bool part) -> bool {
-        const int slot = (2 * t) % NS;
-        if (!mbar_wait_w(bar_kv_full + slot, ((2 * t) / NS) & 1, abort_flag)) return false;
-        if (part) {
-          tc_fence_after();
-          const uint32_t klo = k_lo0 + slot * tile16;
+        for (int w = 0; w < LPE / 2; ++w) {
+          const int ld = LPE * t + w, slot = ld % NS;
+          if (!mbar_wait_w(bar_kv_full + slot, (ld / NS) & 1, abort_flag)) return false;
+          if (part && (!kv2 || w == i)) {
+            tc_fence_after();
+            const uint32_t klo = k_lo0 + slot * tile16;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            constexpr uint32_t kChunk16 = CHUNK_BYTES >> 4;
-            const uint32_t off = (kk >> 2) * kChunk16 + (kk & 3) * 2;
-            mma_ss_w(s_dst, q_lo + off, desc_hi, klo + off, desc_hi, IDESC_S, kk > 0);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              constexpr uint32_t kChunk16 = CHUNK_BYTES >> 4;
+              const uint32_t off = (kk >> 2) * kChunk16 + (kk & 3) * 2;
+              mma_ss_w(s_dst, q_lo + off, desc_hi, klo + off, desc_hi, IDESC_S, kk > 0);
+            }
+            tc_commit_w(bar_s_full + i);
           }
-          tc_commit_w(bar_s_full + i);
+          tc_commit_w(bar_kv_empty + slot);
         }
-        tc_commit_w(bar_kv_empty + slot);
         return true;
       };
-      // O_i += P_i V_t (if visited), then release V_t's slot.  The slot's load is awaited
-      // even when this sub-tile skips the entry: a release may only follow the load of the
-      // same use, so neither thread can release a slot's next use before the other has
-      // released the current one (the empty barrier counts two arrivals per use).
+      // O_i += P_i V_t (if visited), then release the V slots of entry t (as above).
       auto issue_pv = [&](int t, bool part) -> bool {
-        const int slot = (2 * t + 1) % NS;
-        if (!mbar_wait_w(bar_kv_full + slot, ((2 * t + 1) / NS) & 1, abort_flag)) return false;
-        if (part) {
-          // P arrives in FA_FWD_P_PARTS parts of kv columns; a part's MMAs start while the
-          // softmax warps still compute the next.
-          const uint32_t vlo = v_lo0 + slot * tile16;
-          const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
-          constexpr int KPP = kBN / 16 / FA_FWD_P_PARTS;  // K steps per part
+        for (int w = 0; w < LPE / 2; ++w) {
+          const int ld = LPE * t + LPE / 2 + w, slot = ld % NS;
+          if (!mbar_wait_w(bar_kv_full + slot, (ld / NS) & 1, abort_flag)) return false;
+          if (part && (!kv2 || w == i)) {
+            // P arrives in FA_FWD_P_PARTS parts of kv columns; a part's MMAs start while the
+            // softmax warps still compute the next.
+            const uint32_t vlo = v_lo0 + slot * tile16;
+            const uint32_t acc0 = pv_count > 0 ? 1u : 0u;
+            constexpr int KPP = kBN / 16 / FA_FWD_P_PARTS;  // K steps per part
 #pragma unroll
-          for (int hh = 0; hh < FA_FWD_P_PARTS; ++hh) {
-            if (!mbar_wait_w(bar_p_full + FA_FWD_P_PARTS * i + hh, p_phase, abort_flag)) return false;
-            tc_fence_after();
+            for (int hh = 0; hh < FA_FWD_P_PARTS; ++hh) {
+              if (!mbar_wait_w(bar_p_full + FA_FWD_P_PARTS * i + hh, p_phase, abort_flag)) return false;
+              tc_fence_after();
 #pragma unroll
-            for (int kk = KPP * hh; kk < KPP * hh + KPP; ++kk)
-              mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+              for (int kk = KPP * hh; kk < KPP * hh + KPP; ++kk)
+                mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+            }
+            p_phase ^= 1;
+            ++pv_count;
+            if (t == last_t) tc_commit_w(bar_o_full + i);
           }
-          p_phase ^= 1;
-          ++pv_count;
-          if (t == last_t) tc_commit_w(bar_o_full + i);
+          tc_commit_w(bar_kv_empty + slot);
         }
-        tc_commit_w(bar_kv_empty + slot);
         return true;
       };
 
@@ -334,6 +352,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const int q_row = (i ? qt1 : qt0) * kBM + r;
+    const int h = i ? h1 : h0;  // this sub-tile's head
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
     const uint32_t tS = t_lane + TM_S0 + 128 * i;
     const uint32_t tO = t_lane + TM_O0 + D * i;
@@ -537,7 +556,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
     if (q_row < a.Tq)
-      a.lse[(int64_t)bh * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
+      a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
     tc_fence_before();
   }
 
@@ -563,14 +582,20 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   const int npairs = (a.bt.nq + 1) / 2;
   // Q tiles per CTA (tile_cfg bits 0-1): two unless asked otherwise, or unless pairs would
   // leave most of the SMs idle and single tiles at least double the CTAs.
-  int tpc = (tile_cfg & 3) == FA_TILE_Q1 ? 1 : 2;
+  int tpc = (tile_cfg & 3) == FA_TILE_Q1 ? 1 : ((tile_cfg & 3) == FA_TILE_HEADS2 ? 3 : 2);
+  if (tpc == 3 && a.H % 2) return cudaErrorInvalidValue;  // head pairs need an even head count
   if ((tile_cfg & 3) == 0) {
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if ((int64_t)npairs * a.B * a.H * 2 <= sms && a.bt.nq > 1) tpc = 1;
+    // Irregular per-tile masks (tile tables, evaluated bitmasks, unsorted document ids) give
+    // adjacent q tiles different kv lists: head pairs keep both sub-tiles busy on every entry.
+    const bool irregular = (a.mask.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) ||
+                           ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
+    if (irregular && a.H % 2 == 0) tpc = 3;
+    else if ((int64_t)npairs * a.B * a.H * 2 <= sms && a.bt.nq > 1) tpc = 1;
   }
-  const dim3 grid((unsigned)((tpc == 2 ? npairs : a.bt.nq) * a.B * a.H));
+  const dim3 grid((unsigned)((tpc == 2 ? npairs : a.bt.nq) * a.B * (tpc == 3 ? a.H / 2 : a.H)));
   const int sk = score_kind_of(a.score.flags);
   // Strict softmax turns pay off when the tensor cores bound the loop (head dim 128, no
   // score_mod, no per-element mask predicate); a heavier softmax runs better with both

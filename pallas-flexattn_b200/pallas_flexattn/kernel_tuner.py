@@ -180,8 +180,8 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
     fastest of each (replacing the reference's static choice, kernel_tuner.py:11-65).
 
     Forward candidates: K/V pipeline depth (``fwd_stages``, entries in flight; 0 = as deep as
-    shared memory holds) x Q tiles per CTA (two 128-row tiles sharing each K/V load, or one)
-    x softmax schedule (concurrent warpgroups, or strict turns when there is no score_mod).
+    shared memory holds) x launch shape (two 128-row Q tiles of one head sharing each K/V
+    load, one Q tile, or one Q tile of two heads walking the same kv list) x softmax schedule (concurrent warpgroups, or strict turns when there is no score_mod).
     Backward candidates: Q/dO pipeline depth (``bwd_stages``).  Each is timed with CUDA events
     over ``iters`` calls; depths the kernel cannot fit are skipped.  The entry is keyed by
     (GPU, dtype, shapes, mask flags and window, score flags); ``flash_attention`` and friends
@@ -202,8 +202,9 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
     scheds = [L.FA_TILE_SOFTMAX_CONCURRENT] + ([L.FA_TILE_SOFTMAX_TURNS] if plan.sspec.flags == 0 else [])
     fwd_res: Dict[str, float] = {}
     for ns in fwd_stages:
-        for tiles in (L.FA_TILE_Q2, L.FA_TILE_Q1):
-            for sch in (scheds if tiles == L.FA_TILE_Q2 else [L.FA_TILE_SOFTMAX_CONCURRENT]):
+        shapes = (L.FA_TILE_Q2, L.FA_TILE_Q1) + ((L.FA_TILE_HEADS2,) if q.shape[1] % 2 == 0 else ())
+        for tiles in shapes:
+            for sch in (scheds if tiles != L.FA_TILE_Q1 else [L.FA_TILE_SOFTMAX_CONCURRENT]):
                 plan.fwd_stages, plan.fwd_tile_cfg = ns, tiles | sch
                 try:
                     ms = _time(lambda: _run_fwd(plan, q, k, v), iters)
