@@ -202,7 +202,8 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
         (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")))
       return rc;
-    if (p->tile_cfg & ~15) return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
+    if ((p->tile_cfg & ~63) || (p->tile_cfg & 48) == 48)
+      return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
     cudaError_t e = launch_fwd_tc(a, tq, tk, tv, p->tile_cfg, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_fwd (tcgen05)");
     return FA_OK;

@@ -38,11 +38,16 @@ namespace {
 
 constexpr int kBM = 128;          // rows of one Q sub-tile
 constexpr int kBN = 128;          // rows of one K/V tile
-constexpr int kFwdThreads = 384;  // 3 warpgroups: 2 softmax + (producer, MMA, 2 idle)
-// setmaxnreg split: the launch gives every thread 168 registers (384 x 168 = 64512);
-// the softmax warpgroups take 216 and the control warpgroup keeps 72 (2*128*216 + 128*72
-// = 64512).  launch_fwd_tc checks the launch allocation before every launch.
-constexpr int kRegsSoftmax = 216, kRegsCtl = 72;
+// SPLIT = softmax warps per row quadrant and sub-tile: 1 (thread = row, 128 columns) or 2
+// (two warps of the same TMEM lane quadrant share each row, 64 columns each).
+//   SPLIT 1: 384 threads = 2 softmax warpgroups + control; the launch gives 168 registers a
+//            thread (384 x 168 = 64512), setmaxnreg moves softmax to 216, control to 72.
+//   SPLIT 2: 640 threads = 4 softmax warpgroups + control; 96 at launch (640 x 96 = 61440),
+//            softmax 104, control 64 (512 x 104 + 128 x 64 = 61440).
+// launch_fwd_tc checks the launch allocation against the split before every launch.
+template <int SPLIT> struct FwdShape;
+template <> struct FwdShape<1> { static constexpr int threads = 384, regs_softmax = 216, regs_ctl = 72; };
+template <> struct FwdShape<2> { static constexpr int threads = 640, regs_softmax = 104, regs_ctl = 64; };
 // Of every 4 exponential pairs in a full tile, this many run as a polynomial on the FMA
 // pipes instead of the MUFU pipe.
 #ifndef FA_FWD_EXP_EMU
@@ -63,24 +68,27 @@ constexpr int kRegsSoftmax = 216, kRegsCtl = 72;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 struct FwdSmemLayout {
-  int tile_bytes, q_off, kv_off, bar_off, misc_off, cls_off, ent_off, total;
+  int tile_bytes, q_off, kv_off, bar_off, misc_off, xch_off, cls_off, ent_off, total;
 };
 
-__host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv) {
+// xch: with SPLIT 2, the partner warps' partial row maxima (double-buffered by kv entry
+// parity) and, at the end, partial row sums: [2 parity][2 sub-tile][2 half][128] fp32.
+__host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv, int split = 1) {
   FwdSmemLayout L;
   L.tile_bytes = kBM * D * 2;
   L.q_off = 0;
   L.kv_off = 2 * L.tile_bytes;
   L.bar_off = L.kv_off + ns * L.tile_bytes;
-  L.misc_off = L.bar_off + (2 * ns + 10 + 2 * FA_FWD_P_PARTS) * 8;
-  L.cls_off = L.misc_off + 16;
+  L.misc_off = L.bar_off + (2 * ns + 10 + 2 * FA_FWD_P_PARTS + 8) * 8;
+  L.xch_off = L.misc_off + 16;
+  L.cls_off = L.xch_off + (split == 2 ? 2 * 2 * 2 * 128 * 4 : 0);
   L.ent_off = L.cls_off + 4 * nkv;
   L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
   return L;
 }
 
-template <int D, int SK>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+template <int D, int SK, int SPLIT>
+__global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int pingpong, const int tpc) {
   constexpr int CHUNK_BYTES = kBM * 64 * 2;  // one 64-column, 128-byte-swizzled panel
@@ -88,10 +96,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr uint32_t TM_S0 = 0, TM_O0 = 256;
   constexpr uint32_t IDESC_S = make_idesc_bf16(kBM, kBN, 0, 0);
   constexpr uint32_t IDESC_PV = make_idesc_bf16(kBM, D, 0, 1);
+  constexpr int NT = FwdShape<SPLIT>::threads;
+  constexpr int kWarpProd = 8 * SPLIT, kWarpMma0 = kWarpProd + 1;  // issuers kWarpMma0 + i; kWarpMma0 owns TMEM
+  static_assert(SPLIT == 1 || FA_FWD_P_PARTS == 2, "with split rows each half publishes one part of P");
 
   const int NS = a.num_stages;
   const int nkv = a.bt.nkv;
-  const FwdSmemLayout L = fwd_smem_layout(D, NS, nkv);
+  const FwdSmemLayout L = fwd_smem_layout(D, NS, nkv, SPLIT);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -106,6 +117,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* bar_o_full = bar_p_full + 2 * FA_FWD_P_PARTS;  // [2]
   uint64_t* bar_teardown = bar_o_full + 2;     // [2]
   uint64_t* bar_turn = bar_teardown + 2;       // [2] softmax ping-pong
+  uint64_t* bar_pair = bar_turn + 2;           // [2][4]: the two warps sharing rows (SPLIT 2)
+  float* xch = reinterpret_cast<float*>(smem + L.xch_off);
   int* misc = reinterpret_cast<int*>(smem + L.misc_off);
   volatile int* abort_flag = misc;             // misc[0]
   int* n_entries_s = misc + 1;
@@ -136,7 +149,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int LPE = kv2 ? 4 : 2;     // loads per kv entry
 
   // ---------------------------------------------------------------- setup
-  if (warp == 8 && lane == 0) {
+  if (warp == kWarpProd && lane == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_kv_full + s, 1);
@@ -149,19 +162,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     mbar_init(bar_teardown, 1);
     mbar_init(bar_teardown + 1, 1);
-    mbar_init(bar_turn, 128);
-    mbar_init(bar_turn + 1, 128);
+    mbar_init(bar_turn, 128 * SPLIT);
+    mbar_init(bar_turn + 1, 128 * SPLIT);
+    for (int k = 0; k < 8; ++k) mbar_init(bar_pair + k, 64);
     misc[0] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
-  if (warp == 9) {
+  if (warp == kWarpMma0) {
     tmem_alloc(tmem_base_s, 512);
     tmem_relinquish();
   }
-  for (int j = tid; j < nkv; j += kFwdThreads) cls[j] = 0;
+  for (int j = tid; j < nkv; j += NT) cls[j] = 0;
   __syncthreads();
 
   // Mark the kv tiles each sub-tile visits: bits 0-1 sub-tile 0, bits 2-3 sub-tile 1;
@@ -172,19 +186,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (qt >= a.bt.nq) continue;
       const int64_t row = table_head(a.bt, b, i ? h1 : h0) * a.bt.nq + qt;
       const int np = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[row] : 0;
-      for (int e = tid; e < np; e += kFwdThreads) {
+      for (int e = tid; e < np; e += NT) {
         const int j = a.bt.kv_indices[row * a.bt.kv_cap + e];
         if (j >= 0 && j < nkv) atomicOr(&cls[j], 1 << (2 * i));
       }
       const int nf = a.bt.full_kv_num_blocks ? a.bt.full_kv_num_blocks[row] : 0;
-      for (int e = tid; e < nf; e += kFwdThreads) {
+      for (int e = tid; e < nf; e += NT) {
         const int j = a.bt.full_kv_indices[row * a.bt.kv_cap + e];
         if (j >= 0 && j < nkv) atomicOr(&cls[j], 2 << (2 * i));
       }
     }
   }
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kWarpProd) {
     int base = 0;
     for (int j0 = 0; j0 < nkv; j0 += 32) {
       const int j = j0 + lane;
@@ -208,9 +222,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t tmem_base = *tmem_base_s;
   const int n_ent = *n_entries_s;
 
-  if (warp >= 8) {
-  setmaxnreg_dec<kRegsCtl>();
-  if (warp == 8) {
+  if (warp >= kWarpProd) {
+  setmaxnreg_dec<FwdShape<SPLIT>::regs_ctl>();
+  if (warp == kWarpProd) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_ent > 0) {
       const bool has1 = qt1 < a.bt.nq;
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mbar_wait(bar_kv_full + s, (last / NS) & 1, &never);
       }
     }
-  } else if (warp == 9 || warp == 10) {
+  } else if (warp == kWarpMma0 || warp == kWarpMma0 + 1) {
     // ---------------------------------------------------------------- MMA issuers
     // One issuing thread per Q sub-tile (warp 9: sub-tile 0, warp 10: sub-tile 1), so each
     // thread's serial chain of waits, MMAs and commits covers half the work.  Both walk
@@ -254,7 +268,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // 2), so a slot is released only after both sub-tiles' MMAs that read it retired.
     // The whole warp runs the loop with warp-uniform values (descriptors stay in uniform
     // registers); elect.sync picks the lane that issues each tcgen05 instruction.
-    const int i = warp - 9;
+    const int i = warp - kWarpMma0;
     if (n_ent > 0) {
       const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
       int last_t = -1;
@@ -318,7 +332,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               tc_fence_after();
 #pragma unroll
               for (int kk = KPP * hh; kk < KPP * hh + KPP; ++kk)
-                mma_ts_w(o_dst, s_dst + kk * 8, vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
+                // P of K step kk: kv columns 16kk.. as bf16 pairs; with split rows half h's
+                // 64 columns sit at the start of its own S columns (64h)
+                mma_ts_w(o_dst, s_dst + (SPLIT == 2 ? (kk >> 2) * 64 + (kk & 3) * 8 : kk * 8),
+                         vlo + kk * (2048 >> 4), desc_hi, IDESC_PV, kk > 0 ? 1u : acc0);
             }
             p_phase ^= 1;
             ++pv_count;
@@ -346,23 +363,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __syncwarp();
   }
   } else {
-    setmaxnreg_inc<kRegsSoftmax>();
-    // ---------------------------------------------------------------- softmax (thread = row)
-    const int i = warp >> 2;
+    setmaxnreg_inc<FwdShape<SPLIT>::regs_softmax>();
+    // ---------------------------------------------------------------- softmax
+    // SPLIT 1: thread = row, all 128 kv columns of a tile.  SPLIT 2: the two warps of a
+    // sub-tile that read the same TMEM lane quadrant (w and w + 4 of its 8 warps) share each
+    // row: half 0 takes kv columns 0-63, half 1 columns 64-127, and they exchange the partial
+    // row maxima per kv entry (and the partial row sums at the end) through shared memory,
+    // so two warps per SM sub-partition and sub-tile keep the exponentials flowing.  Each
+    // half writes its P into the start of its own S columns and publishes it as one part.
+    constexpr int NC = kBN / SPLIT;  // kv columns per thread
+    constexpr int DO = D / SPLIT;    // O columns per thread (rescale, epilogue)
+    const int i = warp / (4 * SPLIT);
+    const int half = SPLIT == 2 ? (warp >> 2) & 1 : 0;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const int q_row = (i ? qt1 : qt0) * kBM + r;
     const int h = i ? h1 : h0;  // this sub-tile's head
     const uint32_t t_lane = tmem_base + ((uint32_t)(wq * 32) << 16);
-    const uint32_t tS = t_lane + TM_S0 + 128 * i;
-    const uint32_t tO = t_lane + TM_O0 + D * i;
+    const uint32_t tS = t_lane + TM_S0 + 128 * i + NC * half;  // this thread's S columns (P goes to their start)
+    const uint32_t tO = t_lane + TM_O0 + D * i + DO * half;    // this thread's O columns
+    uint64_t* pair_bar = bar_pair + 4 * i + wq;
     const ScoreCtx sc = make_score_ctx(a.score, a.scale, h, a.Tkv);
     const MaskCtx mc = make_mask_ctx(a.mask, b, a.Tkv);
     const int qg = q_row + mc.q_off;  // global position of this row (mask and score mods)
     const int dq_val = (mc.flags & FA_MASK_DOCUMENT) && q_row < a.Tq ? __ldg(mc.doc_q + qg) : 0;
     // Causal, window and the Tkv bound intersect to one allowed kv interval [row_lo, row_hi]
-    // per row; partial tiles test it with two compares.  Document and tile-table predicates
-    // (if enabled) are evaluated per element on top.
+    // per row; partial tiles test it with two compares.  Document, tile-table and bitmask
+    // predicates (if enabled) are evaluated per element on top.
     int row_lo = mc.kv_off, row_hi = mc.Tkv - 1;  // global kv positions
     if (mc.flags & FA_MASK_CAUSAL) row_hi = min(row_hi, qg);
     if (mc.flags & FA_MASK_WINDOW) {
@@ -380,6 +407,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const bool per_elem_mask =
         (mc.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
 
+    // Partner exchange (SPLIT 2): round k writes this thread's value to buffer k & 1, waits
+    // for both warps on the pair barrier, reads the partner's.  A buffer is rewritten two
+    // rounds later, after the partner has passed the round in between, so it has been read.
+    uint32_t xround = 0;
+    auto exchange = [&](float v) -> float {
+      float* buf = xch + (size_t)(((xround & 1) * 2 + i) * 2) * 128;
+      buf[half * 128 + r] = v;
+      mbar_arrive(pair_bar);
+      const bool got = mbar_wait(pair_bar, xround & 1, abort_flag);
+      ++xround;
+      return got ? buf[(1 - half) * 128 + r] : v;
+    };
+
     // Turn-taking is compiled only where the host may enable it (no score_mod).
     constexpr bool PP = SK == SC_NONE;
     float row_max = -INFINITY, row_sum = 0.f;
@@ -389,12 +429,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int t = 0; t < n_ent; ++t) {
       const int e = entries[t];
       const int code = (e >> (24 + 2 * i)) & 3;
-      // Ping-pong (when enabled): the two softmax warpgroups take strict turns (0, 1, 0, 1, ...)
-      // for their exponential loops, one turn per kv entry each, visited or not, so one
-      // warpgroup's exponentials run while the tensor cores work on the other sub-tile's PV and
-      // next S, and the row max (FMA pipe) overlaps the other warpgroup's exponentials (MUFU).
-      // Turn k of warpgroup 0 needs warpgroup 1's (k-1)-th hand-over; turn k of warpgroup 1
-      // needs warpgroup 0's k-th.
+      // Ping-pong (when enabled): the two sub-tiles' softmax warps take strict turns (0, 1, 0,
+      // 1, ...) for their exponential loops, one turn per kv entry each, visited or not, so one
+      // sub-tile's exponentials run while the tensor cores work on the other sub-tile's PV and
+      // next S, and the row max (FMA pipe) overlaps the other sub-tile's exponentials (MUFU).
+      // Turn k of sub-tile 0 needs sub-tile 1's (k-1)-th hand-over; turn k of sub-tile 1 needs
+      // sub-tile 0's k-th.
       const uint32_t turn_parity = i == 0 ? ((t & 1) ^ 1) : (t & 1);
       if (!code) {
         if (PP && pingpong) {
@@ -403,57 +443,56 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         continue;
       }
-      const int kvg0 = (e & 0xFFFFFF) * kBN + mc.kv_off;  // global position of the tile's first key
+      // global position of this thread's first key in the tile
+      const int kvg0 = (e & 0xFFFFFF) * kBN + mc.kv_off + NC * half;
       if (!mbar_wait(bar_s_full + i, s_phase, abort_flag)) { ok = false; break; }
       s_phase ^= 1;
       tc_fence_after();
-      float x[kBN];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(tS + 0, r0);
-        tmem_ld32(tS + 32, r1);
-        tmem_ld32(tS + 64, r2);
-        tmem_ld32(tS + 96, r3);
+      float x[NC];
+#pragma unroll
+      for (int c0 = 0; c0 < NC; c0 += 64) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tS + c0, r0);
+        tmem_ld32(tS + c0 + 32, r1);
         tmem_ld_wait();
-        reg_pin(r0); reg_pin(r1); reg_pin(r2); reg_pin(r3);
+        reg_pin(r0); reg_pin(r1);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          x[c] = __uint_as_float(r0[c]);
-          x[32 + c] = __uint_as_float(r1[c]);
-          x[64 + c] = __uint_as_float(r2[c]);
-          x[96 + c] = __uint_as_float(r3[c]);
+          x[c0 + c] = __uint_as_float(r0[c]);
+          x[c0 + 32 + c] = __uint_as_float(r1[c]);
         }
       }
       // Without a score_mod the mask and the max work on the raw dot products (the
       // scale is positive) and the scale folds into the exponent's FFMA.
       if constexpr (SK != SC_NONE) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) x[c] = score_log2<SK>(x[c], qg, kvg0 + c, sc);
+        for (int c = 0; c < NC; ++c) x[c] = score_log2<SK>(x[c], qg, kvg0 + c, sc);
       }
       if (code & 1) {
         const unsigned span = (unsigned)(row_hi - row_lo);
         const int clo = row_lo - kvg0;
 #pragma unroll
-        for (int c = 0; c < kBN; ++c)
+        for (int c = 0; c < NC; ++c)
           if ((unsigned)(c - clo) > span || row_hi < row_lo) x[c] = -INFINITY;
         if (per_elem_mask) {
 #pragma unroll
-          for (int c = 0; c < kBN; ++c)
+          for (int c = 0; c < NC; ++c)
             if (!mask_ok(mc, qg, kvg0 + c, dq_val)) x[c] = -INFINITY;
         }
       }
-      // Row max with three-input max: 8 accumulators over columns 0-119, then 120-127.
-      static_assert(kBN == 128, "the max tree below covers 128 columns");
+      // Row max with three-input max: 8 accumulators over columns 0 .. NC-9, then the last 8.
+      static_assert(NC == 128 || NC == 64, "the max tree below covers 64 or 128 columns");
       float m8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) m8[k] = fmax3f(x[k], x[8 + k], x[16 + k]);
 #pragma unroll
-      for (int c = 24; c < 120; c += 16)
+      for (int c = 24; c <= NC - 24; c += 16)
 #pragma unroll
         for (int k = 0; k < 8; ++k) m8[k] = fmax3f(m8[k], x[c + k], x[c + 8 + k]);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], x[120 + k]);
+      for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], x[NC - 8 + k]);
       float mloc = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      if constexpr (SPLIT == 2) mloc = fmaxf(mloc, exchange(mloc));  // the row's max over all 128 columns
       if constexpr (SK == SC_NONE) mloc *= sc.k_log2;
       if (PP && pingpong && !mbar_wait(bar_turn + i, turn_parity, abort_flag)) { ok = false; break; }
       float alpha = 1.f;
@@ -465,12 +504,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float m_use = (row_max == -INFINITY) ? 0.f : row_max;
       const float2 kk2 = make_float2(SK == SC_NONE ? sc.k_log2 : 1.f, SK == SC_NONE ? sc.k_log2 : 1.f);
       const float2 nm2 = make_float2(-m_use, -m_use);
-      // Rescale O before any of this entry's P is published (the PV MMAs that read the
-      // first half may start before the second is computed); PV(t-1) has retired, since S(t)
-      // was committed after it.
+      // Rescale O (this thread's DO columns) before any of this entry's P is published (the PV
+      // MMAs that read the first part may start before the second is computed); PV(t-1) has
+      // retired, since S(t) was committed after it.
       if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < DO; c0 += 32) {
           uint32_t ov[32];
           tmem_ld32(tO + c0, ov);
           tmem_ld_wait();
@@ -484,8 +523,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         make_float2(0.f, 0.f)};
       // Full tiles hold no -inf, so some exponentials may take the polynomial path.
       const bool emu = (code & 1) == 0;
+      constexpr int PPT = FA_FWD_P_PARTS / SPLIT;  // parts of P this thread publishes
+      constexpr int PW = NC / PPT;                 // kv columns per published part
 #pragma unroll
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
+      for (int c0 = 0; c0 < NC; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
@@ -501,14 +542,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #endif
         }
         tmem_st16(tS + (c0 >> 1), pk);
-        constexpr int PW = kBN / FA_FWD_P_PARTS;  // kv columns per published part
         if ((c0 + 32) % PW == 0) {  // a part of P is written: publish it to the PV MMAs
           tmem_st_wait();
           tc_fence_before();
-          mbar_arrive(bar_p_full + FA_FWD_P_PARTS * i + c0 / PW);
+          mbar_arrive(bar_p_full + FA_FWD_P_PARTS * i + half * PPT + c0 / PW);
         }
       }
-      if (PP && pingpong) mbar_arrive(bar_turn + (1 - i));  // exponentials issued: the other warpgroup's turn
+      if (PP && pingpong) mbar_arrive(bar_turn + (1 - i));  // exponentials issued: the other sub-tile's turn
       const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
       const float2 s4 = __fadd2_rn(s01, s23);
       const float sum = s4.x + s4.y;
@@ -518,6 +558,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (!ok) {
       report_status(a.status, FA_ERR_TIMEOUT);
       *abort_flag = 1;
+    }
+    // The row's sum over all 128 columns of every tile (both halves scaled by the same maxima).
+    if constexpr (SPLIT == 2) {
+      if (ok && processed > 0) row_sum += exchange(row_sum);
     }
 
     // ---------------------------------------------------------------- epilogue
@@ -533,9 +577,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const bool live = row_sum > 0.f;
     const float inv = live ? 1.f / row_sum : 0.f;
     __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
-                          (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t;
+                          (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t + DO * half;
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
+    for (int c0 = 0; c0 < DO; c0 += 32) {
       uint32_t ov[32];
       if (have_o) {
         tmem_ld32(tO + c0, ov);
@@ -555,13 +599,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
       }
     }
-    if (q_row < a.Tq)
+    if (q_row < a.Tq && half == 0)
       a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
     tc_fence_before();
   }
 
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kWarpMma0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
@@ -576,9 +620,19 @@ int fwd_tc_max_stages(int D, int nkv) {
   return best;
 }
 
-cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           int tile_cfg, cudaStream_t stream) {
-  const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv).total;
+  AttnArgs a = a_in;
+  // Rows split over two softmax warps (tile_cfg bits 4-5).  Chosen by default only for the
+  // tanh softcap, where two MUFU operations per element leave one warp per row latency-bound
+  // (cfg5: 196 -> 243 TFLOP/s with head pairs); with a lighter softmax the partner exchange
+  // and the 104-register budget cost more than the second warp gains (cfg2: 838 -> 613).
+  const int sk_kind = score_kind_of(a.score.flags);
+  const int split = (tile_cfg & 48) == FA_TILE_ROWS_SPLIT ? 2
+                    : ((tile_cfg & 48) == 0 && sk_kind == SC_SOFTCAP) ? 2 : 1;
+  while (a.num_stages > 2 && fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total > 227 * 1024) --a.num_stages;
+  const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const int npairs = (a.bt.nq + 1) / 2;
   // Q tiles per CTA (tile_cfg bits 0-1): two unless asked otherwise, or unless pairs would
   // leave most of the SMs idle and single tiles at least double the CTAs.
@@ -611,19 +665,23 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
   int pingpong = FA_FWD_PINGPONG;
 #endif
   if (tpc == 1) pingpong = 0;
-  auto go = [&](auto kern) -> cudaError_t {
+  auto go = [&](auto kern, auto shape) -> cudaError_t {
     // The register split must fit the launch allocation, or setmaxnreg.inc would wait forever.
+    using S = decltype(shape);
     cudaFuncAttributes fa_attr;
     cudaError_t e = cudaFuncGetAttributes(&fa_attr, kern);
     if (e != cudaSuccess) return e;
-    if (fa_attr.numRegs * kFwdThreads < 2 * 128 * kRegsSoftmax + 128 * kRegsCtl) return cudaErrorInvalidConfiguration;
+    const int softmax_threads = S::threads - 128;
+    if (fa_attr.numRegs * S::threads < softmax_threads * S::regs_softmax + 128 * S::regs_ctl)
+      return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kFwdThreads, smem, stream>>>(tq, tk, tv, a, pingpong, tpc);
+    kern<<<grid, S::threads, smem, stream>>>(tq, tk, tv, a, pingpong, tpc);
     return cudaGetLastError();
   };
-#define FA_FWD_CASE(DD, SKK) \
-  if (a.D == DD && sk == SKK) return go(fwd_tc_kernel<DD, SKK>);
+#define FA_FWD_CASE(DD, SKK)                                                             \
+  if (a.D == DD && sk == SKK)                                                            \
+    return split == 2 ? go(fwd_tc_kernel<DD, SKK, 2>, FwdShape<2>{}) : go(fwd_tc_kernel<DD, SKK, 1>, FwdShape<1>{});
   FA_FWD_CASE(128, SC_NONE)
   FA_FWD_CASE(128, SC_ALIBI)
   FA_FWD_CASE(128, SC_SOFTCAP)

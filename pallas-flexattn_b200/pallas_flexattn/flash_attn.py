@@ -54,7 +54,7 @@ DEFAULT_NUM_WARPS = 4
 DEFAULT_NUM_STAGES = 3
 TC_TILE = 128
 
-_TABLE_CACHE: "OrderedDict[tuple, BlockTables]" = OrderedDict()
+_TABLE_CACHE: "OrderedDict[tuple, tuple[MaskSpec, BlockTables]]" = OrderedDict()
 _TABLE_CACHE_MAX = 64
 _STATUS: dict = {}
 
@@ -84,16 +84,19 @@ def clear_table_cache() -> None:
 
 def _tables_for(spec: MaskSpec, B: int, Tq: int, Tkv: int, bq: int, bkv: int, device,
                 offsets: tuple = (0, 0)) -> BlockTables:
+    # The key names the spec's tensors (document ids, tile table, bitmask) by id(); the entry
+    # keeps the spec, and so those tensors, alive, so no new tensor can take a cached id while
+    # the entry exists and hit tables built for another mask.
     key = (spec.key(), B if spec.depends_on_batch else 1, Tq, Tkv, bq, bkv, str(device), tuple(offsets))
-    bt = _TABLE_CACHE.get(key)
-    if bt is None:
+    hit = _TABLE_CACHE.get(key)
+    if hit is None:
         bt = build_tables_from_spec(spec, B, Tq, Tkv, bq, bkv, device, offsets=offsets)
-        _TABLE_CACHE[key] = bt
+        _TABLE_CACHE[key] = (spec, bt)
         while len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
             _TABLE_CACHE.popitem(last=False)
-    else:
-        _TABLE_CACHE.move_to_end(key)
-    return bt
+        return bt
+    _TABLE_CACHE.move_to_end(key)
+    return hit[1]
 
 
 _DTYPES = {torch.bfloat16: L.FA_DTYPE_BF16, torch.float32: L.FA_DTYPE_F32}

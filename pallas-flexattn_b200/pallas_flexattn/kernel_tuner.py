@@ -181,7 +181,8 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
 
     Forward candidates: K/V pipeline depth (``fwd_stages``, entries in flight; 0 = as deep as
     shared memory holds) x launch shape (two 128-row Q tiles of one head sharing each K/V
-    load, one Q tile, or one Q tile of two heads walking the same kv list) x softmax schedule (concurrent warpgroups, or strict turns when there is no score_mod).
+    load, one Q tile, or one Q tile of two heads walking the same kv list) x softmax schedule
+    x softmax warps per row (one, or two sharing its 128 columns) (concurrent warpgroups, or strict turns when there is no score_mod).
     Backward candidates: Q/dO pipeline depth (``bwd_stages``).  Each is timed with CUDA events
     over ``iters`` calls; depths the kernel cannot fit are skipped.  The entry is keyed by
     (GPU, dtype, shapes, mask flags and window, score flags); ``flash_attention`` and friends
@@ -205,12 +206,14 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
         shapes = (L.FA_TILE_Q2, L.FA_TILE_Q1) + ((L.FA_TILE_HEADS2,) if q.shape[1] % 2 == 0 else ())
         for tiles in shapes:
             for sch in (scheds if tiles != L.FA_TILE_Q1 else [L.FA_TILE_SOFTMAX_CONCURRENT]):
-                plan.fwd_stages, plan.fwd_tile_cfg = ns, tiles | sch
-                try:
-                    ms = _time(lambda: _run_fwd(plan, q, k, v), iters)
-                except L.FlexAttnError:
-                    continue
-                fwd_res[json.dumps([ns, tiles | sch])] = ms
+                for rows in (L.FA_TILE_ROWS_WHOLE, L.FA_TILE_ROWS_SPLIT):
+                    cfg = tiles | sch | rows
+                    plan.fwd_stages, plan.fwd_tile_cfg = ns, cfg
+                    try:
+                        ms = _time(lambda: _run_fwd(plan, q, k, v), iters)
+                    except L.FlexAttnError:
+                        continue
+                    fwd_res[json.dumps([ns, cfg])] = ms
     if not fwd_res:
         raise RuntimeError("autotune: no forward candidate ran")
     best_f = json.loads(min(fwd_res, key=fwd_res.get))

@@ -59,7 +59,7 @@ def test_autotune_caches_and_is_used(tmp_path, monkeypatch, D):
         assert_close(n, a.float().cpu().numpy(), b)
 
 
-@pytest.mark.parametrize("tile_cfg", [1 | 4, 1 | 8, 2 | 4, 2, 3 | 4, 3 | 8, 3])
+@pytest.mark.parametrize("tile_cfg", [1 | 4, 1 | 8, 2 | 4, 2, 3 | 4, 3 | 8, 3, 1 | 4 | 16, 1 | 8 | 16, 2 | 16, 3 | 8 | 16])
 def test_forward_launch_shapes_agree(tile_cfg):
     """Every forward launch shape computes the same attention (ragged length; grouped
     queries with two query heads per K/V head, so head pairs share their K/V loads)."""
@@ -79,8 +79,8 @@ def test_forward_launch_shapes_agree(tile_cfg):
     np.testing.assert_allclose(lse.cpu().numpy(), rl, atol=2e-3, rtol=1e-4)
 
 
-@pytest.mark.parametrize("tile_cfg", [3 | 4, 3 | 8, 0])
-@pytest.mark.parametrize("case", ["tiles_softcap_d64", "lambda_d128", "causal_d128"])
+@pytest.mark.parametrize("tile_cfg", [3 | 4, 3 | 8, 0, 3 | 4 | 16, 1 | 4 | 16, 1 | 8 | 16])
+@pytest.mark.parametrize("case", ["tiles_softcap_d64", "lambda_d128", "causal_d128", "window_alibi_d128"])
 def test_head_pair_launch_shape(tile_cfg, case):
     """One Q tile of two heads per CTA with two distinct K/V heads per entry (K0, K1, V0, V1
     in the ring): irregular tile tables, an evaluated lambda mask and plain causal, against
@@ -96,6 +96,9 @@ def test_head_pair_launch_shape(tile_cfg, case):
         mm = pf.and_masks(pf.causal_mask, pf.tile_mask(table, 128))
         om = O.and_(O.causal, O.tile_table(table, 128))
         score, omods = pf.softcap_score_mod(30.0), (O.softcap(30.0),)
+    elif case == "window_alibi_d128":
+        mm, om = pf.sliding_window_mask(300, 0), O.sliding_window(300, 0)
+        score, omods = pf.alibi_score_mod(4), (O.alibi(O.alibi_slopes(4)),)
     elif case == "lambda_d128":
         mm = om = lambda qi, ki: (((qi * 7 + ki * 3) % 11 < 4) | (qi == ki)) & (qi >= ki)  # noqa: E731
     else:

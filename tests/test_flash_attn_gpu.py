@@ -363,3 +363,23 @@ def test_arbitrary_callable_inside_and_masks_with_score_mod():
     om = O.and_(O.sliding_window(300, 0), lambda q, kv: (kv % 4) != 1)
     q, k, v, do = inputs((2, 2, 768, 128), (2, 2, 768, 128), torch.bfloat16, seed=5)
     check_all(q, k, v, do, mm, om, pf.softcap_score_mod(20.0), (O.softcap(20.0),))
+
+
+def test_fresh_tile_masks_never_reuse_cached_tables():
+    """Block tables are cached under the mask's tensors' ids; a mask built after an earlier one
+    was freed (its tile table may get the same id) must still get its own tables."""
+    import gc
+
+    T = 640
+    q, k, v, do = inputs((1, 2, T, 64), (1, 2, T, 64), torch.bfloat16, seed=3)
+    qf, kf, vf = (t.float().cpu().numpy().astype(np.float64) for t in (q, k, v))
+    for trial in range(6):
+        rng = np.random.default_rng(100 + trial)
+        table = (rng.random((5, 5)) < 0.5).astype(np.uint8)
+        np.fill_diagonal(table, 1)
+        mm = pf.and_masks(pf.causal_mask, pf.tile_mask(table, 128))
+        o, _ = pf.flash_attention_fwd(q, k, v, mm)
+        ro, _ = O.mha_reference(qf, kf, vf, O.and_(O.causal, O.tile_table(table, 128)))
+        close(f"o (trial {trial})", o, ro, torch.bfloat16)
+        del mm, o
+        gc.collect()
