@@ -112,6 +112,12 @@ int check_common(int dtype, int B, int H, int Hkv, int Tq, int Tkv, int D, const
     return fail(FA_ERR_INVALID, "document mask without document ids");
   if ((m.flags & FA_MASK_TILE_TABLE) && (!m.tile_table || m.table_block <= 0 || m.table_cols <= 0))
     return fail(FA_ERR_INVALID, "tile-table mask without a table");
+  // the kernels index the table by position, up to the last (padded) 128-row tile
+  if ((m.flags & FA_MASK_TILE_TABLE) &&
+      ((int64_t)m.table_rows * m.table_block < (int64_t)m.q_offset + (Tq + 127) / 128 * 128 ||
+       (int64_t)m.table_cols * m.table_block < (int64_t)m.kv_offset + (Tkv + 127) / 128 * 128))
+    return fail(FA_ERR_INVALID, "tile table of %d x %d cells of %d does not cover %d x %d positions (rounded up "
+                "to 128)", m.table_rows, m.table_cols, m.table_block, m.q_offset + Tq, m.kv_offset + Tkv);
   if (m.flags & ~(FA_MASK_CAUSAL | FA_MASK_WINDOW | FA_MASK_DOCUMENT | FA_MASK_TILE_TABLE | FA_MASK_DOC_SORTED |
                   FA_MASK_BITMASK))
     return fail(FA_ERR_INVALID, "unknown mask flags 0x%x", m.flags);

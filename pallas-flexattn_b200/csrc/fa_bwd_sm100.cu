@@ -472,8 +472,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       q_lo = max(q_lo, f);
       q_hi = min(q_hi, l);
     }
-    const bool per_elem_mask =
-        (mc.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
+    // A tile table whose cells cover whole 128 x 128 tiles (cell size a multiple of 128, offsets
+    // multiples of 128) is tested once per partial step instead of per element.
+    const bool table_aligned = (mc.flags & FA_MASK_TILE_TABLE) && !(mc.table_block % 128) && !(mc.q_off % 128) &&
+                               !(mc.kv_off % 128);
+    const bool per_elem_mask = ((mc.flags & FA_MASK_TILE_TABLE) && !table_aligned) || (mc.flags & FA_MASK_BITMASK) ||
+                               ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
     bool ok = true;
     for (int t = 0; t < n_ent && ok; ++t) {
       const int e = entries[t];
@@ -519,9 +523,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (partial) {
           const unsigned span = (unsigned)(q_hi - q_lo);
           const int clo = q_lo - qg0;
+          bool kill = q_hi < q_lo;
+          if (table_aligned)
+            kill = kill || !__ldg(mc.table + (qg0 / mc.table_block) * mc.table_cols + kvg / mc.table_block);
 #pragma unroll
           for (int c = 0; c < 32; ++c)
-            if ((unsigned)(c - clo) > span || q_hi < q_lo) p[32 * hh + c] = 0.f;
+            if ((unsigned)(c - clo) > span || kill) p[32 * hh + c] = 0.f;
           if (per_elem_mask) {
 #pragma unroll
             for (int c = 0; c < 32; ++c) {

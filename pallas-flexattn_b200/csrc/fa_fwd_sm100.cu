@@ -404,8 +404,15 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       row_lo = max(row_lo, f);
       row_hi = min(row_hi, l);
     }
-    const bool per_elem_mask =
-        (mc.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) || ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
+    // A tile table whose cells cover whole 128 x 128 tiles (cell size a multiple of 128, offsets
+    // multiples of 128) is tested once per partial tile instead of per element: a tile lies in
+    // one cell.
+    const bool table_aligned = (mc.flags & FA_MASK_TILE_TABLE) && !(mc.table_block % kBN) && !(mc.q_off % kBN) &&
+                               !(mc.kv_off % kBN);
+    const bool table_per_elem = (mc.flags & FA_MASK_TILE_TABLE) && !table_aligned;
+    const bool per_elem_mask = table_per_elem || (mc.flags & FA_MASK_BITMASK) ||
+                               ((mc.flags & FA_MASK_DOCUMENT) && !doc_iv);
+    // From here on only row_lo, row_hi, qg, dq_val and per_elem_mask of the mask context stay live.
 
     // Partner exchange (SPLIT 2): round k writes this thread's value to buffer k & 1, waits
     // for both warps on the pair barrier, reads the partner's.  A buffer is rewritten two
@@ -444,7 +451,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
         continue;
       }
       // global position of this thread's first key in the tile
-      const int kvg0 = (e & 0xFFFFFF) * kBN + mc.kv_off + NC * half;
+      const int kvg0 = (e & 0xFFFFFF) * kBN + a.mask.kv_offset + NC * half;
       if (!mbar_wait(bar_s_full + i, s_phase, abort_flag)) { ok = false; break; }
       s_phase ^= 1;
       tc_fence_after();
@@ -471,13 +478,20 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       if (code & 1) {
         const unsigned span = (unsigned)(row_hi - row_lo);
         const int clo = row_lo - kvg0;
+        bool kill = row_hi < row_lo;  // the row has no allowed key in any tile
+        if (table_aligned)
+          kill = kill || !__ldg(a.mask.tile_table + (qg / a.mask.table_block) * a.mask.table_cols +
+                                kvg0 / a.mask.table_block);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
-          if ((unsigned)(c - clo) > span || row_hi < row_lo) x[c] = -INFINITY;
+          if ((unsigned)(c - clo) > span || kill) x[c] = -INFINITY;
         if (per_elem_mask) {
+          // Rebuilt from the kernel parameters (constant bank) on the partial tiles that need
+          // it, so its pointers and bounds hold no registers across the kv loop.
+          const MaskCtx pm = make_mask_ctx(a.mask, b, a.Tkv);
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (!mask_ok(mc, qg, kvg0 + c, dq_val)) x[c] = -INFINITY;
+            if (!mask_ok(pm, qg, kvg0 + c, dq_val)) x[c] = -INFINITY;
         }
       }
       // Row max with three-input max: 8 accumulators over columns 0 .. NC-9, then the last 8.
@@ -508,49 +522,68 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       // MMAs that read the first part may start before the second is computed); PV(t-1) has
       // retired, since S(t) was committed after it.
       if (processed > 0 && __any_sync(0xffffffffu, rescale)) {
+        if constexpr (SPLIT == 1) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < DO; c0 += 32) {
-          uint32_t ov[32];
-          tmem_ld32(tO + c0, ov);
-          tmem_ld_wait();
-          reg_pin(ov);
+          for (int c0 = 0; c0 < DO; c0 += 32) {
+            uint32_t ov[32];
+            tmem_ld32(tO + c0, ov);
+            tmem_ld_wait();
+            reg_pin(ov);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-          tmem_st32(tO + c0, ov);
+            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+            tmem_st32(tO + c0, ov);
+          }
+        } else {  // 16 columns at a time: the logits of the tile are live in registers
+#pragma unroll 1
+          for (int c0 = 0; c0 < DO; c0 += 16) {
+            uint32_t ov[16];
+            tmem_ld16(tO + c0, ov);
+            tmem_ld_wait();
+            reg_pin(ov);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+            tmem_st16(tO + c0, ov);
+          }
         }
       }
-      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                        make_float2(0.f, 0.f)};
+      // Partial sums: four accumulators with whole rows, two with split rows (registers).
+      constexpr int NSUM = SPLIT == 2 ? 2 : 4;
+      float2 sum2[NSUM];
+#pragma unroll
+      for (int k = 0; k < NSUM; ++k) sum2[k] = make_float2(0.f, 0.f);
       // Full tiles hold no -inf, so some exponentials may take the polynomial path.
       const bool emu = (code & 1) == 0;
       constexpr int PPT = FA_FWD_P_PARTS / SPLIT;  // parts of P this thread publishes
       constexpr int PW = NC / PPT;                 // kv columns per published part
+      constexpr int CW = SPLIT == 2 ? 16 : 32;     // kv columns per TMEM store of P
 #pragma unroll
-      for (int c0 = 0; c0 < NC; c0 += 32) {
-        uint32_t pk[16];
+      for (int c0 = 0; c0 < NC; c0 += CW) {
+        uint32_t pk[CW / 2];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < CW; c += 2) {
           const float2 y = __ffma2_rn(make_float2(x[c0 + c], x[c0 + c + 1]), kk2, nm2);
           float2 p;
           if (((c >> 1) & 3) < FA_FWD_EXP_EMU && emu) p = exp2_poly2(y);
           else p = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-          sum2[(c >> 1) & 3] = __fadd2_rn(sum2[(c >> 1) & 3], p);
+          sum2[(c >> 1) % NSUM] = __fadd2_rn(sum2[(c >> 1) % NSUM], p);
 #if FA_FWD_INT_PACK
           pk[c >> 1] = pack_bf16x2_int(p.x, p.y);
 #else
           pk[c >> 1] = pack_bf16x2(p.x, p.y);
 #endif
         }
-        tmem_st16(tS + (c0 >> 1), pk);
-        if ((c0 + 32) % PW == 0) {  // a part of P is written: publish it to the PV MMAs
+        if constexpr (CW == 32) tmem_st16(tS + (c0 >> 1), pk);
+        else tmem_st8(tS + (c0 >> 1), pk);
+        if ((c0 + CW) % PW == 0) {  // a part of P is written: publish it to the PV MMAs
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(bar_p_full + FA_FWD_P_PARTS * i + half * PPT + c0 / PW);
         }
       }
       if (PP && pingpong) mbar_arrive(bar_turn + (1 - i));  // exponentials issued: the other sub-tile's turn
-      const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
-      const float2 s4 = __fadd2_rn(s01, s23);
+      float2 s4 = sum2[0];
+#pragma unroll
+      for (int k = 1; k < NSUM; ++k) s4 = __fadd2_rn(s4, sum2[k]);
       const float sum = s4.x + s4.y;
       row_sum = row_sum * alpha + sum;
       ++processed;
@@ -623,13 +656,11 @@ int fwd_tc_max_stages(int D, int nkv) {
 cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           int tile_cfg, cudaStream_t stream) {
   AttnArgs a = a_in;
-  // Rows split over two softmax warps (tile_cfg bits 4-5).  Chosen by default only for the
-  // tanh softcap, where two MUFU operations per element leave one warp per row latency-bound
-  // (cfg5: 196 -> 243 TFLOP/s with head pairs); with a lighter softmax the partner exchange
-  // and the 104-register budget cost more than the second warp gains (cfg2: 838 -> 613).
-  const int sk_kind = score_kind_of(a.score.flags);
-  const int split = (tile_cfg & 48) == FA_TILE_ROWS_SPLIT ? 2
-                    : ((tile_cfg & 48) == 0 && sk_kind == SC_SOFTCAP) ? 2 : 1;
+  // Rows split over two softmax warps (tile_cfg bits 4-5) only when asked for (the tuner
+  // measures both): with the 104-register budget of a split-row thread and the partner
+  // exchange, whole rows measured faster on every benchmark config (cfg2 847 vs 733, cfg5
+  // 326 vs 295 TFLOP/s).
+  const int split = (tile_cfg & 48) == FA_TILE_ROWS_SPLIT ? 2 : 1;
   while (a.num_stages > 2 && fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total > 227 * 1024) --a.num_stages;
   const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;

@@ -383,3 +383,18 @@ def test_fresh_tile_masks_never_reuse_cached_tables():
         close(f"o (trial {trial})", o, ro, torch.bfloat16)
         del mm, o
         gc.collect()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_dense_block_lists_with_a_tile_table_mask(D):
+    """Reference-style block lists that visit every tile, with a tile-table mask_mod: every
+    listed tile is partial, so the kernels must apply the table to tiles whose cell is zero
+    (tested once per tile when the cells cover whole 128 x 128 tiles)."""
+    T = 768
+    table = W.random_tile_table(6, 0.35, seed=9)
+    mm = pf.and_masks(pf.causal_mask, pf.tile_mask(table, 128))
+    n = T // 128
+    bm = pf.BlockMask(torch.full((n,), n, dtype=torch.int32), torch.arange(n, dtype=torch.int32).repeat(n, 1),
+                      128, T, T, None, mm)
+    q, k, v, do = inputs((1, 2, T, D), (1, 2, T, D), torch.bfloat16, seed=D)
+    check_all(q, k, v, do, mm, O.and_(O.causal, O.tile_table(table, 128)), block_mask=bm)
