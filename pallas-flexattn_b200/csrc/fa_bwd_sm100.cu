@@ -517,9 +517,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld_wait();
         reg_pin(s);
         const int qg0 = q0 + 32 * hh + mc.q_off;  // global position of column 0 of this group
+        if constexpr (SK == SC_ALIBI) {
+          // slope * (kv - q) log2-scaled as a per-group base minus the unrolled column index
+          // times the slope: no integer-to-float conversion per element
+          const float alibi0 = sc.slope_log2 * (float)(kvg - qg0);
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          p[32 * hh + c] = ex2_approx(score_log2<SK>(__uint_as_float(s[c]), qg0 + c, kvg, sc) - l2[c]);
+          for (int c = 0; c < 32; ++c)
+            p[32 * hh + c] = ex2_approx(
+                fmaf(__uint_as_float(s[c]), sc.k_log2, fmaf(-(float)c, sc.slope_log2, alibi0)) - l2[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            p[32 * hh + c] = ex2_approx(score_log2<SK>(__uint_as_float(s[c]), qg0 + c, kvg, sc) - l2[c]);
+        }
         if (partial) {
           const unsigned span = (unsigned)(q_hi - q_lo);
           const int clo = q_lo - qg0;

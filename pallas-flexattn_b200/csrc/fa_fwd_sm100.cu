@@ -469,11 +469,25 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
           x[c0 + 32 + c] = __uint_as_float(r1[c]);
         }
       }
-      // Without a score_mod the mask and the max work on the raw dot products (the
-      // scale is positive) and the scale folds into the exponent's FFMA.
+      // Without a score_mod the mask and the max work on the raw dot products, with the softcap
+      // on the raw tanh values (both scales are positive), and the scale folds into the
+      // exponent's FFMA.
       if constexpr (SK != SC_NONE) {
+        const float alibi0 = sc.slope_log2 * (float)(kvg0 - qg);  // ALiBi term of column 0
+        const float tanh_k = sc.scale * sc.inv_cap;                 // softcap: tanh argument scale
 #pragma unroll
-        for (int c = 0; c < NC; ++c) x[c] = score_log2<SK>(x[c], qg, kvg0 + c, sc);
+        for (int c = 0; c < NC; ++c) {
+          if constexpr (SK == SC_ALIBI) {
+            // slope * (kv - q) log2-scaled, as a per-tile base plus the unrolled column
+            // index times the slope: two FFMAs, no integer-to-float conversion per element
+            x[c] = fmaf(x[c], sc.k_log2, fmaf((float)c, sc.slope_log2, alibi0));
+          } else if constexpr (SK == SC_SOFTCAP) {
+            // tanh only: cap * log2(e) > 0 scales the max and folds into the exponent's FFMA
+            x[c] = fast_tanh(x[c] * tanh_k);
+          } else {
+            x[c] = score_log2<SK>(x[c], qg, kvg0 + c, sc);
+          }
+        }
       }
       if (code & 1) {
         const unsigned span = (unsigned)(row_hi - row_lo);
@@ -507,7 +521,10 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], x[NC - 8 + k]);
       float mloc = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       if constexpr (SPLIT == 2) mloc = fmaxf(mloc, exchange(mloc));  // the row's max over all 128 columns
-      if constexpr (SK == SC_NONE) mloc *= sc.k_log2;
+      // Scale folded into the exponent (no score_mod: softmax scale; softcap: cap * log2(e)).
+      constexpr bool FOLD = SK == SC_NONE || SK == SC_SOFTCAP;
+      const float kfold = SK == SC_NONE ? sc.k_log2 : (SK == SC_SOFTCAP ? sc.cap_log2 : 1.f);
+      if constexpr (FOLD) mloc *= kfold;
       if (PP && pingpong && !mbar_wait(bar_turn + i, turn_parity, abort_flag)) { ok = false; break; }
       float alpha = 1.f;
       const bool rescale = mloc > row_max + kRescaleThreshold;
@@ -516,7 +533,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
         row_max = mloc;
       }
       const float m_use = (row_max == -INFINITY) ? 0.f : row_max;
-      const float2 kk2 = make_float2(SK == SC_NONE ? sc.k_log2 : 1.f, SK == SC_NONE ? sc.k_log2 : 1.f);
+      const float2 kk2 = make_float2(kfold, kfold);
       const float2 nm2 = make_float2(-m_use, -m_use);
       // Rescale O (this thread's DO columns) before any of this entry's P is published (the PV
       // MMAs that read the first part may start before the second is computed); PV(t-1) has
