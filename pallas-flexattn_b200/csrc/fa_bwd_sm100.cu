@@ -141,8 +141,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // One CTA per (kv tile j, b, kv head hk); with grouped-query attention it walks the q
   // tiles of all G query heads of the group, and dK/dV sum over them.
-  const int bhk = blockIdx.x % (a.B * a.Hkv);
-  const int j = blockIdx.x / (a.B * a.Hkv);  // kv tile; low j first (the most q tiles under causal masks)
+  int j, bhk;  // kv tile (low j first: the most q tiles under causal masks) and (b, K/V head)
+  grid_unit_head((int)blockIdx.x, a.bt.nkv, a.B * a.Hkv, &j, &bhk);
   const int b = bhk / a.Hkv, hk = bhk % a.Hkv;
   const int Tq_pad = (a.Tq + 127) / 128 * 128;
 

@@ -195,6 +195,23 @@ struct AttnArgs {
   int* status;
 };
 
+// Heads per grid group (see grid_unit_head); 0 = one group of all heads.
+#ifndef FA_HEAD_GROUP
+#define FA_HEAD_GROUP 8
+#endif
+
+// CTA -> (work unit, head) with the heads in groups of FA_HEAD_GROUP: the grid walks group by
+// group, and inside a group unit-major (unit 0 of every head of the group, then unit 1, ...),
+// so the CTAs resident at one time share a few heads' K/V, Q, dO and dQ rows in L2 instead
+// of spreading over every head, while the heaviest units of each group still start first.
+__device__ __forceinline__ void grid_unit_head(int x, int nunits, int nheads, int* unit, int* head) {
+  const int hg = (FA_HEAD_GROUP > 0 && FA_HEAD_GROUP < nheads) ? FA_HEAD_GROUP : nheads;
+  const int g = x / (hg * nunits), in = x - g * hg * nunits;
+  const int cnt = min(hg, nheads - g * hg);  // heads in this group (the last may be short)
+  *unit = in / cnt;
+  *head = g * hg + in % cnt;
+}
+
 __device__ __forceinline__ void report_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

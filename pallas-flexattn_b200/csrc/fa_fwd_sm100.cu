@@ -138,8 +138,9 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   const bool hpair = tpc == 3;
   const int HU = hpair ? a.H / 2 : a.H;  // head units per batch row
   const int nunits = tpc == 2 ? (a.bt.nq + 1) >> 1 : a.bt.nq;
-  const int bhu = blockIdx.x % (a.B * HU);
-  const int unit = nunits - 1 - (int)(blockIdx.x / (a.B * HU));  // heaviest (last) q rows first
+  int bhu, urank;
+  grid_unit_head((int)blockIdx.x, nunits, a.B * HU, &urank, &bhu);
+  const int unit = nunits - 1 - urank;  // heaviest (last) q rows first
   const int b = bhu / HU;
   const int h0 = hpair ? 2 * (bhu % HU) : bhu % HU, h1 = hpair ? h0 + 1 : h0;
   const int qt0 = tpc == 2 ? 2 * unit : unit;
