@@ -196,6 +196,10 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
     if (!tc_ok)
       return fail(FA_ERR_UNSUPPORTED,
                   "tcgen05 forward needs bf16, D in {64,128}, 128x128 block tables and 16-byte aligned rows");
+    if ((p->tile_cfg & ~63) || (p->tile_cfg & 48) == 48)
+      return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
+    if ((p->tile_cfg & 3) == FA_TILE_HEADS2 && p->H % 2)
+      return fail(FA_ERR_INVALID, "FA_TILE_HEADS2 pairs heads: H=%d must be even", p->H);
     // num_stages counts K/V entries in flight (the reference's pipelining depth); each
     // entry takes two ring slots (K and V).  0 = as deep as shared memory allows.
     const int max_ns = fwd_tc_max_stages(p->D, p->blocks.nkv);
@@ -208,8 +212,6 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
         (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")))
       return rc;
-    if ((p->tile_cfg & ~63) || (p->tile_cfg & 48) == 48)
-      return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
     cudaError_t e = launch_fwd_tc(a, tq, tk, tv, p->tile_cfg, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_fwd (tcgen05)");
     return FA_OK;

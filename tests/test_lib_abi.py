@@ -111,3 +111,28 @@ def test_ctypes_layout_matches_header(tmp_path):
         assert int(got[f"{s} size"]) == C.sizeof(cls), s
         for f, _ in cls._fields_:
             assert int(got[f"{s}.{f}"]) == getattr(cls, f).offset, f"{s}.{f}"
+
+
+def test_tile_cfg_validation_without_gpu():
+    """Launch-shape requests the forward cannot honour are rejected before any CUDA call."""
+    import torch  # noqa: F401  (ctypes structs only)
+
+    lib = L.lib()
+    p = L.FaFwdParams()
+    p.dtype, p.B, p.H, p.H_kv, p.Tq, p.Tkv, p.D = L.FA_DTYPE_BF16, 1, 3, 3, 256, 256, 128
+    p.scale = 0.088
+    p.blocks.block_q = p.blocks.block_kv = 128
+    p.blocks.nq = p.blocks.nkv = 2
+    p.blocks.num_b = p.blocks.num_h = 1
+    p.blocks.kv_num_blocks = p.blocks.kv_indices = 16  # never dereferenced: validation fails first
+    p.blocks.kv_cap = 2
+    for t in ("q", "k", "v", "o"):
+        setattr(getattr(p, t), "ptr", 4096)
+    p.lse = 4096
+    p.kernel = L.FA_KERNEL_TC
+    p.tile_cfg = L.FA_TILE_HEADS2
+    assert lib.fa_fwd(C.byref(p), None) == L.FA_ERR_INVALID
+    assert b"even" in lib.fa_last_error()
+    p.tile_cfg = L.FA_TILE_ROWS_SPLIT | L.FA_TILE_ROWS_WHOLE
+    assert lib.fa_fwd(C.byref(p), None) == L.FA_ERR_INVALID
+    assert b"tile_cfg" in lib.fa_last_error()
