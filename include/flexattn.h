@@ -142,8 +142,8 @@ typedef struct {
 
 /* Launch shape of the tcgen05 forward (FaFwdParams.tile_cfg), the measured autotuner's
  * choices besides the pipeline depth.  Bits 0-1: Q tiles per CTA; bits 2-3: softmax schedule
- * of the two sub-tiles; bits 4-5: softmax warps per row.  0 in a field = the launcher's
- * per-launch choice. */
+ * of the two sub-tiles; bits 4-5: softmax warps per row; bit 6: kv halves.  0 in a field = the
+ * launcher's per-launch choice. */
 enum {
   FA_TILE_Q2 = 1,                 /* two 128-row Q tiles per CTA sharing each K/V tile load */
   FA_TILE_Q1 = 2,                 /* one Q tile per CTA (twice the CTAs; for small grids) */
@@ -153,6 +153,9 @@ enum {
   FA_TILE_SOFTMAX_TURNS = 8,      /* strict turns per kv tile (no score_mod only) */
   FA_TILE_ROWS_SPLIT = 16,        /* bits 4-5: each softmax row shared by two warps (64 columns each) */
   FA_TILE_ROWS_WHOLE = 32,        /*           one warp per row (128 columns) */
+  FA_TILE_KV_HALVES = 64,         /* bit 6: one Q tile per CTA, its kv list split over the two
+                                     sub-tiles and merged at the end (small grids, long rows);
+                                     shape bits 0-1 must be 0, rows whole */
 };
 
 typedef struct {

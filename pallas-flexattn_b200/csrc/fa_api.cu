@@ -196,8 +196,9 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
     if (!tc_ok)
       return fail(FA_ERR_UNSUPPORTED,
                   "tcgen05 forward needs bf16, D in {64,128}, 128x128 block tables and 16-byte aligned rows");
-    if ((p->tile_cfg & ~63) || (p->tile_cfg & 48) == 48)
-      return fail(FA_ERR_INVALID, "unknown tile_cfg bits 0x%x", p->tile_cfg);
+    if ((p->tile_cfg & ~127) || (p->tile_cfg & 48) == 48 ||
+        ((p->tile_cfg & FA_TILE_KV_HALVES) && ((p->tile_cfg & 3) || (p->tile_cfg & 48) == FA_TILE_ROWS_SPLIT)))
+      return fail(FA_ERR_INVALID, "unknown or conflicting tile_cfg bits 0x%x", p->tile_cfg);
     if ((p->tile_cfg & 3) == FA_TILE_HEADS2 && p->H % 2)
       return fail(FA_ERR_INVALID, "FA_TILE_HEADS2 pairs heads: H=%d must be even", p->H);
     // num_stages counts K/V entries in flight (the reference's pipelining depth); each

@@ -72,8 +72,9 @@ struct FwdSmemLayout {
 };
 
 // xch: with SPLIT 2, the partner warps' partial row maxima (double-buffered by kv entry
-// parity) and, at the end, partial row sums: [2 parity][2 sub-tile][2 half][128] fp32.
-__host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv, int split = 1) {
+// parity) and, at the end, partial row sums: [2 parity][2 sub-tile][2 half][128] fp32; with kv
+// halves, the two sub-tiles' row statistics for the merge ([2 sub-tile][3][128]).
+__host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv, bool xch = false) {
   FwdSmemLayout L;
   L.tile_bytes = kBM * D * 2;
   L.q_off = 0;
@@ -81,7 +82,7 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv,
   L.bar_off = L.kv_off + ns * L.tile_bytes;
   L.misc_off = L.bar_off + (2 * ns + 10 + 2 * FA_FWD_P_PARTS + 8) * 8;
   L.xch_off = L.misc_off + 16;
-  L.cls_off = L.xch_off + (split == 2 ? 2 * 2 * 2 * 128 * 4 : 0);
+  L.cls_off = L.xch_off + (xch ? 2 * 2 * 2 * 128 * 4 : 0);
   L.ent_off = L.cls_off + 4 * nkv;
   L.total = L.ent_off + 4 * nkv + 1024;  // + alignment slack
   return L;
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
 
   const int NS = a.num_stages;
   const int nkv = a.bt.nkv;
-  const FwdSmemLayout L = fwd_smem_layout(D, NS, nkv, SPLIT);
+  const FwdSmemLayout L = fwd_smem_layout(D, NS, nkv, SPLIT == 2 || tpc == 4);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   //      depend on the head), so neither idles when the list is irregular; each entry loads
   //      K and V of both heads, or once when both heads share a K/V head (grouped queries).
   const bool hpair = tpc == 3;
+  const bool kvhalves = tpc == 4;  // one Q tile; sub-tile 0 takes the first half of its kv list, 1 the rest
   const int HU = hpair ? a.H / 2 : a.H;  // head units per batch row
   const int nunits = tpc == 2 ? (a.bt.nq + 1) >> 1 : a.bt.nq;
   int bhu, urank;
@@ -144,7 +146,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   const int b = bhu / HU;
   const int h0 = hpair ? 2 * (bhu % HU) : bhu % HU, h1 = hpair ? h0 + 1 : h0;
   const int qt0 = tpc == 2 ? 2 * unit : unit;
-  const int qt1 = tpc == 2 ? 2 * unit + 1 : (hpair ? unit : a.bt.nq);
+  const int qt1 = tpc == 2 ? 2 * unit + 1 : ((hpair || kvhalves) ? unit : a.bt.nq);
   const int hk0 = h0 / (a.H / a.Hkv), hk1 = h1 / (a.H / a.Hkv);
   const bool kv2 = hk1 != hk0;     // two K/V heads: each entry is K0, K1, V0, V1 (else K, V)
   const int LPE = kv2 ? 4 : 2;     // loads per kv entry
@@ -215,6 +217,21 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       if (c) entries[base + __popc(m & ((1u << lane) - 1u))] = j | (c << 24);
       base += __popc(m);
     }
+    if (kvhalves) {
+      // Both sub-tiles hold the same q tile: the first ceil(n/2) entries go to sub-tile 0, the
+      // rest to sub-tile 1, interleaved (e0, e_A, e1, e_A+1, ...) so the producer's in-order
+      // loads feed both at once.  The reordered list passes through cls[] (free by now).
+      __syncwarp();
+      const int A = (base + 1) >> 1, Bn = base - A;
+      for (int t = lane; t < base; t += 32) {
+        const int src = t < 2 * Bn ? ((t & 1) ? A + (t >> 1) : (t >> 1)) : t - Bn;
+        const int e = entries[src];
+        const int code = (e >> 24) & 3;  // both sub-tiles carry the same code
+        cls[t] = (e & 0xFFFFFF) | ((src < A ? code : code << 2) << 24);
+      }
+      __syncwarp();
+      for (int t = lane; t < base; t += 32) entries[t] = cls[t];
+    }
     if (lane == 0) *n_entries_s = base;
   }
   tc_fence_before();
@@ -228,7 +245,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   if (warp == kWarpProd) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n_ent > 0) {
-      const bool has1 = qt1 < a.bt.nq;
+      const bool has1 = qt1 < a.bt.nq && !kvhalves;  // with kv halves both sub-tiles read Q tile 0
       mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
       for (int i = 0; i < (has1 ? 2 : 1); ++i)
         for (int c = 0; c < NCHUNK; ++c)
@@ -286,7 +303,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       const uint64_t dq_base = make_smem_desc(sQa, 16, 1024, SMEM_SWIZZLE_128B);
       const uint32_t desc_hi = (uint32_t)(dq_base >> 32);
       const uint32_t tile16 = (uint32_t)L.tile_bytes >> 4;
-      const uint32_t q_lo = (uint32_t)dq_base + i * tile16;
+      const uint32_t q_lo = (uint32_t)dq_base + (kvhalves ? 0u : i * tile16);  // kv halves share Q tile 0
       const uint32_t k_lo0 = (uint32_t)make_smem_desc(sKVa, 16, 1024, SMEM_SWIZZLE_128B);
       const uint32_t v_lo0 = (uint32_t)make_smem_desc(sKVa, CHUNK_BYTES, 1024, SMEM_SWIZZLE_128B);
       const uint32_t s_dst = tmem_base + TM_S0 + 128 * i, o_dst = tmem_base + TM_O0 + D * i;
@@ -616,6 +633,77 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     }
 
     // ---------------------------------------------------------------- epilogue
+    bool merged = false;
+    if constexpr (SPLIT == 1) {
+      if (kvhalves) {
+        // The two sub-tiles hold the same rows over the two halves of the kv list: exchange the
+        // row statistics with the partner warp (same lane quadrant, other sub-tile), then sub-tile
+        // i writes output columns [i D/2, (i+1) D/2) of the merged row
+        //   o = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)),  m = max(m0, m1),
+        // reading both sub-tiles' O columns from TMEM (a sub-tile without entries has no O).
+        const bool mine = ok && processed > 0;
+        float* st = xch;  // [2 sub-tile][3 field][128]
+        st[(i * 3 + 0) * 128 + r] = mine ? row_max : -INFINITY;
+        st[(i * 3 + 1) * 128 + r] = mine ? row_sum : 0.f;
+        st[(i * 3 + 2) * 128 + r] = mine ? 1.f : 0.f;
+        mbar_arrive(bar_pair + wq);
+        const bool got = mbar_wait(bar_pair + wq, 0, abort_flag);
+        const float m_p = got ? st[((1 - i) * 3 + 0) * 128 + r] : -INFINITY;
+        const float l_p = got ? st[((1 - i) * 3 + 1) * 128 + r] : 0.f;
+        const bool theirs = got && st[((1 - i) * 3 + 2) * 128 + r] != 0.f;
+        if (!got) {
+          report_status(a.status, FA_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        const float m_m = mine ? row_max : -INFINITY;
+        const float m = fmaxf(m_m, m_p);
+        const float a_m = (m_m == -INFINITY) ? 0.f : ex2_approx(m_m - m);
+        const float a_p = (m_p == -INFINITY) ? 0.f : ex2_approx(m_p - m);
+        const float l = (mine ? row_sum : 0.f) * a_m + l_p * a_p;
+        const bool live = l > 0.f;
+        const float inv = live ? 1.f / l : 0.f;
+        // coefficients and availability of O0 (sub-tile 0) and O1 (sub-tile 1)
+        const float c0f = (i == 0 ? a_m : a_p) * inv, c1f = (i == 1 ? a_m : a_p) * inv;
+        bool have0 = i == 0 ? mine : theirs, have1 = i == 1 ? mine : theirs;
+        if (have0 && !mbar_wait(bar_o_full + 0, 0, abort_flag)) have0 = false;
+        if (have1 && !mbar_wait(bar_o_full + 1, 0, abort_flag)) have1 = false;
+        // tcgen05.ld is warp-wide: read an O only if every lane may
+        have0 = __all_sync(0xffffffffu, have0);
+        have1 = __all_sync(0xffffffffu, have1);
+        tc_fence_after();
+        const int oc0 = i * (D / 2);  // this sub-tile's output columns
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
+                              (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t + oc0;
+        const uint32_t tO0 = t_lane + TM_O0 + oc0, tO1 = t_lane + TM_O0 + D + oc0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D / 2; c0 += 32) {
+          uint32_t u0[32] = {}, u1[32] = {};
+          if (have0) tmem_ld32(tO0 + c0, u0);
+          if (have1) tmem_ld32(tO1 + c0, u1);
+          tmem_ld_wait();
+          reg_pin(u0);
+          reg_pin(u1);
+          if (q_row < a.Tq) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const float x0 = (have0 ? __uint_as_float(u0[c]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c]) * c1f : 0.f);
+              const float x1 =
+                  (have0 ? __uint_as_float(u0[c + 1]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c + 1]) * c1f : 0.f);
+              pk[c >> 1] = pack_bf16x2(x0, x1);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+        if (q_row < a.Tq && i == 0)
+          a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (m + __log2f(l)) * kLn2 : -INFINITY;
+        tc_fence_before();
+        merged = true;
+      }
+    }
+    if (!merged) {
     bool have_o = ok && processed > 0;
     if (have_o) {
       have_o = mbar_wait(bar_o_full + i, 0, abort_flag);
@@ -653,6 +741,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     if (q_row < a.Tq && half == 0)
       a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
     tc_fence_before();
+    }
   }
 
   __syncthreads();
@@ -679,15 +768,13 @@ cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUt
   // exchange, whole rows measured faster on every benchmark config (cfg2 847 vs 733, cfg5
   // 326 vs 295 TFLOP/s).
   const int split = (tile_cfg & 48) == FA_TILE_ROWS_SPLIT ? 2 : 1;
-  while (a.num_stages > 2 && fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total > 227 * 1024) --a.num_stages;
-  const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split).total;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const int npairs = (a.bt.nq + 1) / 2;
   // Q tiles per CTA (tile_cfg bits 0-1): two unless asked otherwise, or unless pairs would
   // leave most of the SMs idle and single tiles at least double the CTAs.
-  int tpc = (tile_cfg & 3) == FA_TILE_Q1 ? 1 : ((tile_cfg & 3) == FA_TILE_HEADS2 ? 3 : 2);
+  int tpc = (tile_cfg & FA_TILE_KV_HALVES) ? 4
+            : (tile_cfg & 3) == FA_TILE_Q1 ? 1 : ((tile_cfg & 3) == FA_TILE_HEADS2 ? 3 : 2);
   if (tpc == 3 && a.H % 2) return cudaErrorInvalidValue;  // head pairs need an even head count
-  if ((tile_cfg & 3) == 0) {
+  if ((tile_cfg & 3) == 0 && !(tile_cfg & FA_TILE_KV_HALVES)) {
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -695,9 +782,18 @@ cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUt
     // adjacent q tiles different kv lists: head pairs keep both sub-tiles busy on every entry.
     const bool irregular = (a.mask.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) ||
                            ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
-    if (irregular && a.H % 2 == 0) tpc = 3;
-    else if ((int64_t)npairs * a.B * a.H * 2 <= sms && a.bt.nq > 1) tpc = 1;
+    // Pairs that would not fill one wave: split each q tile's kv list over the two sub-tiles
+    // instead (twice the CTAs, half the longest chain).  Measured on head shards of cfg2 (causal
+    // S 4096): 128 pair CTAs 431 -> 545 TFLOP/s; with 256 pair CTAs the pairs stay ahead (800 vs
+    // 573), as they do for short rows (cfg3 shards).
+    if ((int64_t)npairs * a.B * a.H < (int64_t)sms && a.bt.nq > 1 && split == 1) tpc = 4;
+    else if (irregular && a.H % 2 == 0) tpc = 3;
   }
+  if (tpc == 4 && split == 2) return cudaErrorInvalidValue;  // kv halves merge whole rows only
+  while (a.num_stages > 2 && fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split == 2 || tpc == 4).total > 227 * 1024)
+    --a.num_stages;
+  const int smem = fwd_smem_layout(a.D, a.num_stages, a.bt.nkv, split == 2 || tpc == 4).total;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const dim3 grid((unsigned)((tpc == 2 ? npairs : a.bt.nq) * a.B * (tpc == 3 ? a.H / 2 : a.H)));
   const int sk = score_kind_of(a.score.flags);
   // Strict softmax turns pay off when the tensor cores bound the loop (head dim 128, no

@@ -20,7 +20,7 @@ FA_SCORE_ALIBI, FA_SCORE_SOFTCAP, FA_SCORE_REL_BIAS = 1, 2, 4
 FA_BLOCK_MASK_EXACT, FA_BLOCK_MASK_REF9 = 0, 1
 FA_NOALLOC_SCRATCH_BYTES = 64 << 20  # static scratch of fa_bwd_noalloc
 FA_TILE_Q2, FA_TILE_Q1, FA_TILE_HEADS2, FA_TILE_SOFTMAX_CONCURRENT, FA_TILE_SOFTMAX_TURNS = 1, 2, 3, 4, 8
-FA_TILE_ROWS_SPLIT, FA_TILE_ROWS_WHOLE = 16, 32
+FA_TILE_ROWS_SPLIT, FA_TILE_ROWS_WHOLE, FA_TILE_KV_HALVES = 16, 32, 64
 
 _i32p = C.POINTER(C.c_int32)
 

@@ -181,7 +181,8 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
 
     Forward candidates: K/V pipeline depth (``fwd_stages``, entries in flight; 0 = as deep as
     shared memory holds) x launch shape (two 128-row Q tiles of one head sharing each K/V
-    load, one Q tile, or one Q tile of two heads walking the same kv list) x softmax schedule
+    load, one Q tile, one Q tile of two heads walking the same kv list, or one Q tile whose kv
+    list is split over the two sub-tiles) x softmax schedule
     x softmax warps per row (one, or two sharing its 128 columns) (concurrent warpgroups, or strict turns when there is no score_mod).
     Backward candidates: Q/dO pipeline depth (``bwd_stages``).  Each is timed with CUDA events
     over ``iters`` calls; depths the kernel cannot fit are skipped.  The entry is keyed by
@@ -203,10 +204,13 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
     scheds = [L.FA_TILE_SOFTMAX_CONCURRENT] + ([L.FA_TILE_SOFTMAX_TURNS] if plan.sspec.flags == 0 else [])
     fwd_res: Dict[str, float] = {}
     for ns in fwd_stages:
-        shapes = (L.FA_TILE_Q2, L.FA_TILE_Q1) + ((L.FA_TILE_HEADS2,) if q.shape[1] % 2 == 0 else ())
+        shapes = (L.FA_TILE_Q2, L.FA_TILE_Q1, L.FA_TILE_KV_HALVES) + (
+            (L.FA_TILE_HEADS2,) if q.shape[1] % 2 == 0 else ())
         for tiles in shapes:
             for sch in (scheds if tiles != L.FA_TILE_Q1 else [L.FA_TILE_SOFTMAX_CONCURRENT]):
-                for rows in (L.FA_TILE_ROWS_WHOLE, L.FA_TILE_ROWS_SPLIT):
+                rows_opts = (L.FA_TILE_ROWS_WHOLE,) if tiles == L.FA_TILE_KV_HALVES else (
+                    L.FA_TILE_ROWS_WHOLE, L.FA_TILE_ROWS_SPLIT)
+                for rows in rows_opts:
                     cfg = tiles | sch | rows
                     plan.fwd_stages, plan.fwd_tile_cfg = ns, cfg
                     try:

@@ -31,7 +31,8 @@ def test_autotune_caches_and_is_used(tmp_path, monkeypatch, D):
     fwd_c = entry["candidates"]["fwd [num_stages, tile_cfg]"]
     assert len(fwd_c) >= 4 and entry["bwd"]["num_stages"] in (2, 3, 4)
     tiles = {cfg[1] & 3 for cfg in map(json.loads, fwd_c)}
-    assert tiles == {L.FA_TILE_Q1, L.FA_TILE_Q2, L.FA_TILE_HEADS2}  # every launch shape was measured
+    assert tiles == {L.FA_TILE_Q1, L.FA_TILE_Q2, L.FA_TILE_HEADS2, 0}  # every launch shape was measured
+    assert any(cfg[1] & L.FA_TILE_KV_HALVES for cfg in map(json.loads, fwd_c))
     assert (tmp_path / "tune.json").exists()
 
     KT.clear_memory_cache()  # the planner reads the entry back from the file
@@ -59,7 +60,8 @@ def test_autotune_caches_and_is_used(tmp_path, monkeypatch, D):
         assert_close(n, a.float().cpu().numpy(), b)
 
 
-@pytest.mark.parametrize("tile_cfg", [1 | 4, 1 | 8, 2 | 4, 2, 3 | 4, 3 | 8, 3, 1 | 4 | 16, 1 | 8 | 16, 2 | 16, 3 | 8 | 16])
+@pytest.mark.parametrize("tile_cfg", [1 | 4, 1 | 8, 2 | 4, 2, 3 | 4, 3 | 8, 3, 1 | 4 | 16, 1 | 8 | 16, 2 | 16, 3 | 8 | 16,
+                                      64 | 4, 64 | 8, 64])
 def test_forward_launch_shapes_agree(tile_cfg):
     """Every forward launch shape computes the same attention (ragged length; grouped
     queries with two query heads per K/V head, so head pairs share their K/V loads)."""
@@ -79,7 +81,7 @@ def test_forward_launch_shapes_agree(tile_cfg):
     np.testing.assert_allclose(lse.cpu().numpy(), rl, atol=2e-3, rtol=1e-4)
 
 
-@pytest.mark.parametrize("tile_cfg", [3 | 4, 3 | 8, 0, 3 | 4 | 16, 1 | 4 | 16, 1 | 8 | 16])
+@pytest.mark.parametrize("tile_cfg", [3 | 4, 3 | 8, 0, 3 | 4 | 16, 1 | 4 | 16, 1 | 8 | 16, 64 | 4, 64 | 8])
 @pytest.mark.parametrize("case", ["tiles_softcap_d64", "lambda_d128", "causal_d128", "window_alibi_d128"])
 def test_head_pair_launch_shape(tile_cfg, case):
     """One Q tile of two heads per CTA with two distinct K/V heads per entry (K0, K1, V0, V1
