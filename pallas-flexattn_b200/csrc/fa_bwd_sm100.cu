@@ -31,6 +31,7 @@
 // (D = 128) 152 for WG0/WG1, 128 for WG2 (no change), 80 for WG3, or (D = 64) 176 / 80 / 80.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "fa_common.cuh"
@@ -501,6 +502,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // p stays fp32 until dSt is formed; each 32-column group of Pt goes back to TMEM (bf16,
       // into already-read S columns) as soon as it is computed.
       float p[NP];
+      // Softcap at D = 64 (registers to spare): the derivative 1 - t^2 of each element kept from
+      // the P phase as packed fp16 (its 11-bit relative precision on a factor in (0, 1] is
+      // finer than the bf16 rounding of dS that follows), instead of recovering t from p with a
+      // log2 (a third MUFU operation per element) in the dS phase.
+      constexpr bool KEEP_G = SK == SC_SOFTCAP && D == 64;
+      uint32_t g2[KEEP_G ? NP / 2 : 1];
 #pragma unroll
       for (int hh = 0; hh < NP / 32; ++hh) {
         uint32_t s[32];
@@ -525,6 +532,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int c = 0; c < 32; ++c)
             p[32 * hh + c] = ex2_approx(
                 fmaf(__uint_as_float(s[c]), sc.k_log2, fmaf(-(float)c, sc.slope_log2, alibi0)) - l2[c]);
+        } else if constexpr (KEEP_G) {
+          const float tanh_k = sc.scale * sc.inv_cap;
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float t0 = fast_tanh(__uint_as_float(s[c]) * tanh_k);
+            const float t1 = fast_tanh(__uint_as_float(s[c + 1]) * tanh_k);
+            p[32 * hh + c] = ex2_approx(fmaf(sc.cap_log2, t0, -l2[c]));
+            p[32 * hh + c + 1] = ex2_approx(fmaf(sc.cap_log2, t1, -l2[c + 1]));
+            const __half2 g = __floats2half2_rn(fmaf(-t0, t0, 1.f), fmaf(-t1, t1, 1.f));
+            g2[(32 * hh + c) >> 1] = *reinterpret_cast<const uint32_t*>(&g);
+          }
         } else {
 #pragma unroll
           for (int c = 0; c < 32; ++c)
@@ -579,7 +597,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int cc = 32 * hh + c;
           float d0 = p[cc] * (__uint_as_float(dp[c]) - dl32[c]);
           float d1 = p[cc + 1] * (__uint_as_float(dp[c + 1]) - dl32[c + 1]);
-          if constexpr (SK == SC_SOFTCAP || SK == SC_GENERAL) {
+          if constexpr (KEEP_G) {
+            const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&g2[cc >> 1]));
+            d0 *= g.x;
+            d1 *= g.y;
+          } else if constexpr (SK == SC_SOFTCAP || SK == SC_GENERAL) {
             // Softcap derivative 1 - t^2, with t = x / cap_log2 recovered from p = 2^(x - lse2)
             // instead of being held in registers since the P phase.  p = 0 means dS = 0.
             if (sc.flags & FA_SCORE_SOFTCAP) {
