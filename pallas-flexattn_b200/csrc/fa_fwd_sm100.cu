@@ -445,8 +445,8 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
       return got ? buf[(1 - half) * 128 + r] : v;
     };
 
-    // Turn-taking is compiled only where the host may enable it (no score_mod).
-    constexpr bool PP = SK == SC_NONE;
+    // Turn-taking is compiled only where the host may enable it (no score_mod, or ALiBi).
+    constexpr bool PP = SK == SC_NONE || SK == SC_ALIBI;
     float row_max = -INFINITY, row_sum = 0.f;
     uint32_t s_phase = 0;
     int processed = 0;
@@ -797,15 +797,16 @@ cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUt
   const dim3 grid((unsigned)((tpc == 2 ? npairs : a.bt.nq) * a.B * (tpc == 3 ? a.H / 2 : a.H)));
   const int sk = score_kind_of(a.score.flags);
   // Strict softmax turns pay off when the tensor cores bound the loop (head dim 128, no
-  // score_mod, no per-element mask predicate); a heavier softmax runs better with both
-  // warpgroups in flight at once.  tile_cfg bits 2-3 override the choice; with one Q tile
-  // per CTA there is no second warpgroup to take turns with.
+  // score_mod or only ALiBi's one extra FFMA per score, no per-element mask predicate); a
+  // heavier softmax (softcap's tanh) runs better with both warpgroups in flight at once.
+  // tile_cfg bits 2-3 override the choice; with one Q tile per CTA there is no second
+  // warpgroup to take turns with.
 #if FA_FWD_PINGPONG < 0
   const bool per_elem = (a.mask.flags & (FA_MASK_TILE_TABLE | FA_MASK_BITMASK)) ||
                         ((a.mask.flags & FA_MASK_DOCUMENT) && !(a.mask.flags & FA_MASK_DOC_SORTED));
-  int pingpong = a.D == 128 && sk == SC_NONE && !per_elem;
+  int pingpong = a.D == 128 && (sk == SC_NONE || sk == SC_ALIBI) && !per_elem;
   if ((tile_cfg & 12) == FA_TILE_SOFTMAX_CONCURRENT) pingpong = 0;
-  if ((tile_cfg & 12) == FA_TILE_SOFTMAX_TURNS) pingpong = sk == SC_NONE;  // compiled only without a score_mod
+  if ((tile_cfg & 12) == FA_TILE_SOFTMAX_TURNS) pingpong = sk == SC_NONE || sk == SC_ALIBI;  // compiled for these
 #else
   int pingpong = FA_FWD_PINGPONG;
 #endif

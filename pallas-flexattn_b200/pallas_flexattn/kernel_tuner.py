@@ -201,7 +201,8 @@ def autotune(q, k, v, mask_mod=None, score_mod=None, block_mask=None, *,
     if not plan.tc:
         raise ValueError("autotune: only the tcgen05 kernels (bf16, D in {64, 128}) have launch choices")
     key = tune_key(q, k, mask_mod, score_mod)
-    scheds = [L.FA_TILE_SOFTMAX_CONCURRENT] + ([L.FA_TILE_SOFTMAX_TURNS] if plan.sspec.flags == 0 else [])
+    scheds = [L.FA_TILE_SOFTMAX_CONCURRENT] + (
+        [L.FA_TILE_SOFTMAX_TURNS] if plan.sspec.flags in (0, L.FA_SCORE_ALIBI) else [])
     fwd_res: Dict[str, float] = {}
     for ns in fwd_stages:
         shapes = (L.FA_TILE_Q2, L.FA_TILE_Q1, L.FA_TILE_KV_HALVES) + (
