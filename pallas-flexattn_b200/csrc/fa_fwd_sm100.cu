@@ -151,6 +151,45 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   const bool kv2 = hk1 != hk0;     // two K/V heads: each entry is K0, K1, V0, V1 (else K, V)
   const int LPE = kv2 ? 4 : 2;     // loads per kv entry
 
+  // Block tables: the four list lengths (partial and full, per sub-tile) are independent loads,
+  // and each thread fetches its first index of the four lists (taken as one flattened list)
+  // before the set-up barrier, so the table reads cost two round trips that overlap the
+  // set-up instead of a chain of dependent loads per list.
+  int64_t trow0 = 0, trow1 = 0;
+  int tcnt[4] = {0, 0, 0, 0};  // partial list of sub-tile 0, of sub-tile 1; full list of 0, of 1
+  if (qt0 < a.bt.nq) {
+    trow0 = table_head(a.bt, b, h0) * a.bt.nq + qt0;
+    tcnt[0] = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[trow0] : 0;
+    tcnt[2] = a.bt.full_kv_num_blocks ? a.bt.full_kv_num_blocks[trow0] : 0;
+  }
+  if (qt1 < a.bt.nq) {
+    trow1 = table_head(a.bt, b, h1) * a.bt.nq + qt1;
+    tcnt[1] = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[trow1] : 0;
+    tcnt[3] = a.bt.full_kv_num_blocks ? a.bt.full_kv_num_blocks[trow1] : 0;
+  }
+  const int ttot = tcnt[0] + tcnt[1] + tcnt[2] + tcnt[3];
+  // kv tile of flattened entry e and its mark: bits 0-1 sub-tile 0, bits 2-3 sub-tile 1;
+  // code 1 = partial (mask applied), 2 = full
+  auto table_entry = [&](int e, int* mark) -> int {
+    int off = e, l = 0;
+    if (off >= tcnt[0]) {
+      off -= tcnt[0];
+      l = 1;
+      if (off >= tcnt[1]) {
+        off -= tcnt[1];
+        l = 2;
+        if (off >= tcnt[2]) {
+          off -= tcnt[2];
+          l = 3;
+        }
+      }
+    }
+    *mark = (l >= 2 ? 2 : 1) << (2 * (l & 1));
+    return (l >= 2 ? a.bt.full_kv_indices : a.bt.kv_indices)[((l & 1) ? trow1 : trow0) * a.bt.kv_cap + off];
+  };
+  int my_mark = 0;
+  const int my_j = tid < ttot ? table_entry(tid, &my_mark) : -1;
+
   // ---------------------------------------------------------------- setup
   if (warp == kWarpProd && lane == 0) {
     mbar_init(bar_q, 1);
@@ -173,6 +212,13 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    // Q does not depend on the kv lists: its load overlaps the table reads and the set-up.
+    const bool has1 = qt1 < a.bt.nq && !kvhalves;  // with kv halves both sub-tiles read Q tile 0
+    mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
+    for (int i = 0; i < (has1 ? 2 : 1); ++i)
+      for (int c = 0; c < NCHUNK; ++c)
+        tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (i ? qt1 : qt0) * kBM,
+                    i ? h1 : h0, b);
   }
   if (warp == kWarpMma0) {
     tmem_alloc(tmem_base_s, 512);
@@ -181,24 +227,12 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   for (int j = tid; j < nkv; j += NT) cls[j] = 0;
   __syncthreads();
 
-  // Mark the kv tiles each sub-tile visits: bits 0-1 sub-tile 0, bits 2-3 sub-tile 1;
-  // code 1 = partial (mask applied), 2 = full.
-  {
-    for (int i = 0; i < 2; ++i) {
-      const int qt = i ? qt1 : qt0;
-      if (qt >= a.bt.nq) continue;
-      const int64_t row = table_head(a.bt, b, i ? h1 : h0) * a.bt.nq + qt;
-      const int np = a.bt.kv_num_blocks ? a.bt.kv_num_blocks[row] : 0;
-      for (int e = tid; e < np; e += NT) {
-        const int j = a.bt.kv_indices[row * a.bt.kv_cap + e];
-        if (j >= 0 && j < nkv) atomicOr(&cls[j], 1 << (2 * i));
-      }
-      const int nf = a.bt.full_kv_num_blocks ? a.bt.full_kv_num_blocks[row] : 0;
-      for (int e = tid; e < nf; e += NT) {
-        const int j = a.bt.full_kv_indices[row * a.bt.kv_cap + e];
-        if (j >= 0 && j < nkv) atomicOr(&cls[j], 2 << (2 * i));
-      }
-    }
+  // Mark the kv tiles each sub-tile visits (a tile listed twice keeps both marks).
+  if (my_j >= 0 && my_j < nkv) atomicOr(&cls[my_j], my_mark);
+  for (int e = tid + NT; e < ttot; e += NT) {
+    int mark;
+    const int j = table_entry(e, &mark);
+    if (j >= 0 && j < nkv) atomicOr(&cls[j], mark);
   }
   __syncthreads();
   if (warp == kWarpProd) {
@@ -244,13 +278,7 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
   setmaxnreg_dec<FwdShape<SPLIT>::regs_ctl>();
   if (warp == kWarpProd) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0 && n_ent > 0) {
-      const bool has1 = qt1 < a.bt.nq && !kvhalves;  // with kv halves both sub-tiles read Q tile 0
-      mbar_arrive_expect_tx(bar_q, (has1 ? 2 : 1) * L.tile_bytes);
-      for (int i = 0; i < (has1 ? 2 : 1); ++i)
-        for (int c = 0; c < NCHUNK; ++c)
-          tma_load_4d(sQ + i * L.tile_bytes + c * CHUNK_BYTES, &tm_q, bar_q, c * 64, (i ? qt1 : qt0) * kBM,
-                      i ? h1 : h0, b);
+    if (lane == 0) {
       bool ok = true;
       int issued = 0;  // loads issued so far: per entry K, V (one K/V head) or K0, K1, V0, V1
       for (int t = 0; t < n_ent && ok; ++t) {
