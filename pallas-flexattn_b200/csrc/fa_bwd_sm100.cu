@@ -147,6 +147,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int b = bhk / a.Hkv, hk = bhk % a.Hkv;
   const int Tq_pad = (a.Tq + 127) / 128 * 128;
 
+  // Block tables of query head g of the group: both list lengths are independent loads, and
+  // each thread fetches its first index of the two lists (taken as one) at once, so the reads
+  // cost two round trips; head 0's overlap the set-up below.
+  struct HeadList {
+    int64_t row;
+    int np, nf, my_i, my_mark;
+  };
+  auto head_list = [&](int g) -> HeadList {
+    HeadList r;
+    r.row = table_head(a.bt, b, hk * G + g) * a.bt.nkv + j;
+    r.np = a.bt.q_num_blocks ? a.bt.q_num_blocks[r.row] : 0;
+    r.nf = a.bt.full_q_num_blocks ? a.bt.full_q_num_blocks[r.row] : 0;
+    r.my_i = -1;
+    r.my_mark = 0;
+    if (tid < r.np) {
+      r.my_i = a.bt.q_indices[r.row * a.bt.q_cap + tid];
+      r.my_mark = 1;
+    } else if (tid < r.np + r.nf) {
+      r.my_i = a.bt.full_q_indices[r.row * a.bt.q_cap + tid - r.np];
+      r.my_mark = 2;
+    }
+    return r;
+  };
+  HeadList hl = head_list(0);
+
   if (warp == kWarpProd && lane == 0) {
     mbar_init(bar_kv, 1);
     for (int s = 0; s < NQS; ++s) {
@@ -174,6 +199,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
+    // This CTA's K and V tiles do not depend on the q lists: their load overlaps the table reads.
+    mbar_arrive_expect_tx(bar_kv, 2 * L.ktile);
+    for (int c = 0; c < NCHUNK; ++c) {
+      tma_load_4d(sK + c * C::PANEL_K, &tm_k, bar_kv, c * 64, j * kBM, hk, b);
+      tma_load_4d(sV + c * C::PANEL_K, &tm_v, bar_kv, c * 64, j * kBM, hk, b);
+    }
   }
   if (warp == kWarpMma) {
     tmem_alloc(tmem_base_s, 512);
@@ -181,21 +212,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   int n_built = 0;  // entries built so far (producer warp)
   for (int g = 0; g < G; ++g) {
-  const int h = hk * G + g;
+  if (g > 0) hl = head_list(g);
   for (int i = tid; i < nq; i += kBwdThreads) cls[i] = 0;
   __syncthreads();
-  {
-    const int64_t row = table_head(a.bt, b, h) * a.bt.nkv + j;
-    const int np = a.bt.q_num_blocks ? a.bt.q_num_blocks[row] : 0;
-    for (int e = tid; e < np; e += kBwdThreads) {
-      const int i = a.bt.q_indices[row * a.bt.q_cap + e];
-      if (i >= 0 && i < nq) atomicOr(&cls[i], 1);
-    }
-    const int nf = a.bt.full_q_num_blocks ? a.bt.full_q_num_blocks[row] : 0;
-    for (int e = tid; e < nf; e += kBwdThreads) {
-      const int i = a.bt.full_q_indices[row * a.bt.q_cap + e];
-      if (i >= 0 && i < nq) atomicOr(&cls[i], 2);
-    }
+  if (hl.my_i >= 0 && hl.my_i < nq) atomicOr(&cls[hl.my_i], hl.my_mark);
+  for (int e = tid + kBwdThreads; e < hl.np + hl.nf; e += kBwdThreads) {
+    const bool full = e >= hl.np;
+    const int i = full ? a.bt.full_q_indices[hl.row * a.bt.q_cap + e - hl.np] : a.bt.q_indices[hl.row * a.bt.q_cap + e];
+    if (i >= 0 && i < nq) atomicOr(&cls[i], full ? 2 : 1);
   }
   __syncthreads();
   if (warp == kWarpProd) {
@@ -235,12 +259,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     setmaxnreg_dec<BwdRegs<D>::ctl>();
     if (warp == kWarpProd) {
       // ---------------------------------------------------------------- TMA producer
-      if (lane == 0 && n_ent > 0) {
-        mbar_arrive_expect_tx(bar_kv, 2 * L.ktile);
-        for (int c = 0; c < NCHUNK; ++c) {
-          tma_load_4d(sK + c * C::PANEL_K, &tm_k, bar_kv, c * 64, j * kBM, hk, b);
-          tma_load_4d(sV + c * C::PANEL_K, &tm_v, bar_kv, c * 64, j * kBM, hk, b);
-        }
+      if (lane == 0) {
         const float* lse2 = a.lse2 + (int64_t)b * a.H * Tq_pad;  // rows of head h at + h * Tq_pad
         const float* dl = a.delta + (int64_t)b * a.H * Tq_pad;
         bool ok = true;
