@@ -208,12 +208,13 @@ int fa_fwd(const FaFwdParams* p, fa_stream_t stream) {
     if (ns < 2) ns = 2;
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q")) ||
         (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
-        (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")))
+        (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")) ||
+        (rc = make_bf16_map(&to, p->o, p->B, p->H, p->Tq, p->D, "o")))
       return rc;
-    cudaError_t e = launch_fwd_tc(a, tq, tk, tv, p->tile_cfg, (cudaStream_t)stream);
+    cudaError_t e = launch_fwd_tc(a, tq, tk, tv, to, p->tile_cfg, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_fwd (tcgen05)");
     return FA_OK;
   }

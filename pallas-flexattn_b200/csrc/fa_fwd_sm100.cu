@@ -91,7 +91,8 @@ __host__ __device__ inline FwdSmemLayout fwd_smem_layout(int D, int ns, int nkv,
 template <int D, int SK, int SPLIT>
 __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs a, const int pingpong, const int tpc) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const AttnArgs a, const int pingpong, const int tpc) {
   constexpr int CHUNK_BYTES = kBM * 64 * 2;  // one 64-column, 128-byte-swizzled panel
   constexpr int NCHUNK = D / 64;
   constexpr uint32_t TM_S0 = 0, TM_O0 = 256;
@@ -743,8 +744,13 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
     }
     const bool live = row_sum > 0.f;
     const float inv = live ? 1.f / row_sum : 0.f;
-    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
-                          (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t + DO * half;
+    // O leaves through this sub-tile's Q buffer, in the 128-byte-swizzled panel layout of the
+    // TMA maps (16-byte chunk c of row r at position c ^ (r & 7)), as one TMA store per 64-column
+    // panel.  The buffer is free: O full follows the sub-tile's last S, and a sub-tile without
+    // entries still waits for its Q load to land before reusing the buffer.
+    const int qt = i ? qt1 : qt0;
+    uint8_t* stage = sQ + i * L.tile_bytes;
+    if (!have_o) mbar_wait(bar_q, 0, abort_flag);
 #pragma unroll 1
     for (int c0 = 0; c0 < DO; c0 += 32) {
       uint32_t ov[32];
@@ -756,18 +762,27 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
 #pragma unroll
         for (int c = 0; c < 32; ++c) ov[c] = 0u;
       }
-      if (q_row < a.Tq) {
-        uint32_t pk[16];
+      uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2)
-          pk[c >> 1] = pack_bf16x2(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
-        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+      for (int c = 0; c < 32; c += 2)
+        pk[c >> 1] = pack_bf16x2(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
+      const int col = DO * half + c0;  // first of these 32 output columns
+      uint8_t* prow = stage + (col >> 6) * CHUNK_BYTES + r * 128;
+      const int ch0 = (col & 63) >> 3;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-      }
+      for (int v = 0; v < 4; ++v)
+        *reinterpret_cast<uint4*>(prow + (((ch0 + v) ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
     }
     if (q_row < a.Tq && half == 0)
       a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (row_max + __log2f(row_sum)) * kLn2 : -INFINITY;
+    fence_proxy_async_smem();  // the staged rows are visible to the TMA (async proxy)
+    named_bar_sync(1 + i, 128 * SPLIT);
+    if (warp == i * 4 * SPLIT && lane == 0 && qt < a.bt.nq) {
+      for (int c = 0; c < NCHUNK; ++c) tma_store_4d(&tm_o, stage + c * CHUNK_BYTES, c * 64, qt * kBM, h, b);
+      bulk_commit_group();
+      bulk_wait_read_all();  // shared memory stays valid until the stores have read it
+    }
     tc_fence_before();
     }
   }
@@ -789,7 +804,7 @@ int fwd_tc_max_stages(int D, int nkv) {
 }
 
 cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          int tile_cfg, cudaStream_t stream) {
+                          const CUtensorMap& to, int tile_cfg, cudaStream_t stream) {
   AttnArgs a = a_in;
   // Rows split over two softmax warps (tile_cfg bits 4-5) only when asked for (the tuner
   // measures both): with the 104-register budget of a split-row thread and the partner
@@ -850,7 +865,7 @@ cudaError_t launch_fwd_tc(const AttnArgs& a_in, const CUtensorMap& tq, const CUt
       return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, S::threads, smem, stream>>>(tq, tk, tv, a, pingpong, tpc);
+    kern<<<grid, S::threads, smem, stream>>>(tq, tk, tv, to, a, pingpong, tpc);
     return cudaGetLastError();
   };
 #define FA_FWD_CASE(DD, SKK)                                                             \

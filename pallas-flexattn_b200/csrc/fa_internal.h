@@ -18,7 +18,7 @@ int make_row_tile_map(CUtensorMap* map, const FaTensor& t, int dtype, int B, int
 // tcgen05 forward (fa_fwd_sm100.cu)
 int fwd_tc_max_stages(int D, int nkv);
 cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          int tile_cfg, cudaStream_t stream);
+                          const CUtensorMap& to, int tile_cfg, cudaStream_t stream);
 
 // tcgen05 backward (fa_bwd_sm100.cu)
 int bwd_tc_max_stages(int D, int nq, int G);  // G = H / H_kv query heads per K/V head

@@ -95,6 +95,20 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// 4-D tiled store shared -> global, tracked by the issuing thread's bulk group.  Elements
+// outside the tensor (rows past T) are not written; coordinates are non-negative and x is a
+// multiple of 64 elements.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+// Barrier among `count` threads (a multiple of 32) of the CTA on named barrier `id` (1-15).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the source buffers of this thread's committed bulk groups have been read.
 __device__ __forceinline__ void bulk_wait_read_all() {
