@@ -310,15 +310,17 @@ int fa_bwd(const FaBwdParams* p, void* workspace, size_t workspace_bytes, fa_str
     int ns = p->num_stages > 0 ? p->num_stages : 2;
     if (ns > max_ns) ns = max_ns;
     a.num_stages = ns;
-    CUtensorMap tq, tk, tv, tdo, tdq;
+    CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
     const int qrows = bwd_tc_q_rows(p->D);
     if ((rc = make_bf16_map(&tq, p->q, p->B, p->H, p->Tq, p->D, "q", qrows)) ||
         (rc = make_bf16_map(&tk, p->k, p->B, p->H_kv, p->Tkv, p->D, "k")) ||
         (rc = make_bf16_map(&tv, p->v, p->B, p->H_kv, p->Tkv, p->D, "v")) ||
         (rc = make_bf16_map(&tdo, p->dout, p->B, p->H, p->Tq, p->D, "dout", qrows)) ||
-        (rc = make_dq_accum_map(&tdq, a.dq_accum, p->B * p->H, p->Tq, p->D)))
+        (rc = make_dq_accum_map(&tdq, a.dq_accum, p->B * p->H, p->Tq, p->D)) ||
+        (rc = make_bf16_map(&tdk, p->dk, p->B, p->H_kv, p->Tkv, p->D, "dk")) ||
+        (rc = make_bf16_map(&tdv, p->dv, p->B, p->H_kv, p->Tkv, p->D, "dv")))
       return rc;
-    e = launch_bwd_tc(a, tq, tk, tv, tdo, tdq, (cudaStream_t)stream);
+    e = launch_bwd_tc(a, tq, tk, tv, tdo, tdq, tdk, tdv, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "fa_bwd (tcgen05)");
   } else if (kernel == FA_KERNEL_SIMT) {
     e = launch_bwd_simt(a, p->dtype, (cudaStream_t)stream);

@@ -24,7 +24,8 @@ cudaError_t launch_fwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtens
 int bwd_tc_max_stages(int D, int nq, int G);  // G = H / H_kv query heads per K/V head
 int bwd_tc_q_rows(int D);         // q rows per step (the Q / dO tensor-map box height)
 cudaError_t launch_bwd_tc(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                          const CUtensorMap& tdo, const CUtensorMap& tdq, cudaStream_t stream);
+                          const CUtensorMap& tdo, const CUtensorMap& tdq, const CUtensorMap& tdk,
+                          const CUtensorMap& tdv, cudaStream_t stream);
 
 // generic CUDA-core kernels (fa_simt.cu)
 cudaError_t launch_fwd_simt(const AttnArgs& a, int dtype, cudaStream_t stream);
