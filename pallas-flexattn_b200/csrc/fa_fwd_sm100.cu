@@ -701,9 +701,11 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
         have1 = __all_sync(0xffffffffu, have1);
         tc_fence_after();
         const int oc0 = i * (D / 2);  // this sub-tile's output columns
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o.ptr) + (int64_t)b * a.o.stride_b +
-                              (int64_t)h * a.o.stride_h + (int64_t)q_row * a.o.stride_t + oc0;
         const uint32_t tO0 = t_lane + TM_O0 + oc0, tO1 = t_lane + TM_O0 + D + oc0;
+        // The merged rows leave through Q tile 0 (both sub-tiles' S MMAs, its only readers, have
+        // retired once both O are complete; without entries the Q load is awaited instead) in the
+        // swizzled TMA layout, then by one TMA store per 64-column panel.
+        mbar_wait(bar_q, 0, abort_flag);
 #pragma unroll 1
         for (int c0 = 0; c0 < D / 2; c0 += 32) {
           uint32_t u0[32] = {}, u1[32] = {};
@@ -712,22 +714,31 @@ __global__ void __launch_bounds__(FwdShape<SPLIT>::threads, 1)
           tmem_ld_wait();
           reg_pin(u0);
           reg_pin(u1);
-          if (q_row < a.Tq) {
-            uint32_t pk[16];
+          uint32_t pk[16];
 #pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              const float x0 = (have0 ? __uint_as_float(u0[c]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c]) * c1f : 0.f);
-              const float x1 =
-                  (have0 ? __uint_as_float(u0[c + 1]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c + 1]) * c1f : 0.f);
-              pk[c >> 1] = pack_bf16x2(x0, x1);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          for (int c = 0; c < 32; c += 2) {
+            const float x0 = (have0 ? __uint_as_float(u0[c]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c]) * c1f : 0.f);
+            const float x1 =
+                (have0 ? __uint_as_float(u0[c + 1]) * c0f : 0.f) + (have1 ? __uint_as_float(u1[c + 1]) * c1f : 0.f);
+            pk[c >> 1] = pack_bf16x2(x0, x1);
           }
+          const int col = oc0 + c0;  // first of these 32 output columns
+          uint8_t* prow = sQ + (col >> 6) * CHUNK_BYTES + r * 128;
+          const int ch0 = (col & 63) >> 3;
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(prow + (((ch0 + v) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
         if (q_row < a.Tq && i == 0)
           a.lse[((int64_t)b * a.H + h) * a.Tq + q_row] = live ? (m + __log2f(l)) * kLn2 : -INFINITY;
+        fence_proxy_async_smem();  // the staged rows are visible to the TMA (async proxy)
+        named_bar_sync(3, 256);    // both sub-tiles' softmax warps
+        if (warp == 0 && lane == 0) {
+          for (int c = 0; c < NCHUNK; ++c) tma_store_4d(&tm_o, sQ + c * CHUNK_BYTES, c * 64, qt0 * kBM, h, b);
+          bulk_commit_group();
+          bulk_wait_read_all();  // shared memory stays valid until the stores have read it
+        }
         tc_fence_before();
         merged = true;
       }

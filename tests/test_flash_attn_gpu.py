@@ -398,3 +398,25 @@ def test_dense_block_lists_with_a_tile_table_mask(D):
                       128, T, T, None, mm)
     q, k, v, do = inputs((1, 2, T, D), (1, 2, T, D), torch.bfloat16, seed=D)
     check_all(q, k, v, do, mm, O.and_(O.causal, O.tile_table(table, 128)), block_mask=bm)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("tile_cfg", [33, 34, 35, 96, 17, 41, 37])
+def test_every_forward_launch_shape(D, tile_cfg):
+    """Each launch shape of the tcgen05 forward (two Q tiles, one, head pairs, kv halves, rows
+    split over two warps, softmax turns or concurrent) against the oracle on a ragged length,
+    so every epilogue (the per-sub-tile TMA store, the kv-halves merge) writes the tail rows
+    right; causal, and bidirectional with ALiBi (which also takes softmax turns)."""
+    from pallas_flexattn import flash_attn as FA
+
+    q, k, v, do = inputs((2, 4, 333, D), (2, 4, 333, D), torch.bfloat16, seed=40 + tile_cfg)
+    for mask_mod, omask, score_mod, omods in ((pf.causal_mask, O.causal, None, ()),
+                                              (None, None, pf.alibi_score_mod(4), (O.alibi(O.alibi_slopes(4)),))):
+        plan = FA._Plan(q, k, v, mask_mod, score_mod, None, 128, 128, 0, None, need_bwd=False)
+        plan.fwd_tile_cfg = tile_cfg
+        o2, lse = FA._run_fwd(plan, q, k, v)
+        torch.cuda.synchronize()
+        check_device_status(DEV)
+        ro, rlse, _ = oracle(q, k, v, do, omask, omods)
+        close("o", o2, ro, torch.bfloat16)
+        np.testing.assert_allclose(lse.cpu().numpy(), rlse, rtol=0, atol=2e-3)
