@@ -115,6 +115,58 @@ __global__ void __launch_bounds__(kRowsPerCta * 32)
   if (lane == 0) lse_acc[row] = mx + logf(tot);
 }
 
+// Vector combine for bf16 parts of D = 64 or 128 (the ring's partial outputs): L = D / 8 lanes
+// per row, a 16-byte load of the part and two of the fp32 accumulator per lane, kMergePasses
+// rows per lane group with every load issued before the first use (the row-per-warp kernel
+// above waits for the two logsumexps before it loads the row).
+constexpr int kMergePasses = 4;
+
+template <int D>
+__global__ void __launch_bounds__(256)
+    lse_merge_bf16_vec_kernel(int rows, float* o_acc, float* lse_acc, const __nv_bfloat16* o_part, int64_t stride,
+                              const float* lse_part) {
+  constexpr int L = D / 8;     // lanes per row
+  constexpr int RPW = 32 / L;  // rows per warp and pass
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / L, c = (lane % L) * 8;
+  const int64_t base = ((int64_t)blockIdx.x * 8 + warp) * (RPW * kMergePasses) + sub;
+  float la[kMergePasses], lb[kMergePasses];
+  uint4 pb[kMergePasses];
+  float4 a0[kMergePasses], a1[kMergePasses];
+#pragma unroll
+  for (int k = 0; k < kMergePasses; ++k) {
+    const int64_t row = base + k * RPW;
+    la[k] = lb[k] = -INFINITY;
+    if (row < rows) {
+      la[k] = lse_acc[row];
+      lb[k] = lse_part[row];
+      pb[k] = *reinterpret_cast<const uint4*>(o_part + row * stride + c);
+      a0[k] = *reinterpret_cast<const float4*>(o_acc + row * D + c);
+      a1[k] = *reinterpret_cast<const float4*>(o_acc + row * D + c + 4);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kMergePasses; ++k) {
+    const int64_t row = base + k * RPW;
+    const float mx = fmaxf(la[k], lb[k]);
+    if (row >= rows || mx == -INFINITY) continue;  // both empty: keep o_acc = 0, lse = -inf
+    const float wa = (la[k] == -INFINITY) ? 0.f : expf(la[k] - mx);
+    const float wb = (lb[k] == -INFINITY) ? 0.f : expf(lb[k] - mx);
+    const float tot = wa + wb;
+    const float ca = wa / tot, cb = wb / tot;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pb[k]);
+    const float2 b0 = __bfloat1622float2(h[0]), b1 = __bfloat1622float2(h[1]), b2 = __bfloat1622float2(h[2]),
+                 b3 = __bfloat1622float2(h[3]);
+    const float4 r0 = make_float4(a0[k].x * ca + b0.x * cb, a0[k].y * ca + b0.y * cb, a0[k].z * ca + b1.x * cb,
+                                  a0[k].w * ca + b1.y * cb);
+    const float4 r1 = make_float4(a1[k].x * ca + b2.x * cb, a1[k].y * ca + b2.y * cb, a1[k].z * ca + b3.x * cb,
+                                  a1[k].w * ca + b3.y * cb);
+    *reinterpret_cast<float4*>(o_acc + row * D + c) = r0;
+    *reinterpret_cast<float4*>(o_acc + row * D + c + 4) = r1;
+    if (lane % L == 0) lse_acc[row] = mx + logf(tot);
+  }
+}
+
 constexpr int kVecPasses = 4;  // rows per lane group in flight
 
 // Vector preprocess for bf16 rows of D = 64 or 128, fused with the zeroing of the fp32 dQ
@@ -261,6 +313,18 @@ cudaError_t launch_dq_convert(const AttnArgs& a, int dtype, cudaStream_t stream)
 
 cudaError_t launch_lse_merge(int rows, int D, float* o_acc, float* lse_acc, const void* o_part, int64_t stride,
                              int dtype, const float* lse_part, cudaStream_t stream) {
+  const bool vec = dtype == FA_DTYPE_BF16 && (D == 64 || D == 128) && stride % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(o_part) & 15) == 0 && (reinterpret_cast<uintptr_t>(o_acc) & 15) == 0;
+  if (vec) {
+    const int per_cta = 8 * (32 / (D / 8)) * kMergePasses;
+    const unsigned vgrid = (unsigned)((rows + per_cta - 1) / per_cta);
+    const auto* op = static_cast<const __nv_bfloat16*>(o_part);
+    if (D == 64)
+      lse_merge_bf16_vec_kernel<64><<<vgrid, 256, 0, stream>>>(rows, o_acc, lse_acc, op, stride, lse_part);
+    else
+      lse_merge_bf16_vec_kernel<128><<<vgrid, 256, 0, stream>>>(rows, o_acc, lse_acc, op, stride, lse_part);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
   if (dtype == FA_DTYPE_F32)
     lse_merge_kernel<float><<<grid, kRowsPerCta * 32, 0, stream>>>(rows, D, o_acc, lse_acc,
