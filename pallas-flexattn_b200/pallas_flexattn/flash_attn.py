@@ -191,6 +191,18 @@ class _Plan:
         self.c_score = sspec.to_c(self.device, H, Tq, Tkv)
         self.c_tables = bt.to_c()
         self.status = device_status(self.device)
+        self._templates = {}  # parameter structs with everything but the tensors, per pass
+        self._ws_bytes = None
+
+    def template(self, cls):
+        """A filled parameter struct of type `cls` (FaFwdParams / FaBwdParams) without tensors;
+        each call copies it (a memcpy) instead of setting every field again."""
+        t = self._templates.get(cls)
+        if t is None:
+            t = cls()
+            self._fill(t)
+            self._templates[cls] = t
+        return cls.from_buffer_copy(t)
 
     def _fill(self, p):
         p.dtype = self.dtype
@@ -208,8 +220,7 @@ class _Plan:
 def _run_fwd(plan: _Plan, q, k, v) -> Tuple[torch.Tensor, torch.Tensor]:
     o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
-    p = L.FaFwdParams()
-    plan._fill(p)
+    p = plan.template(L.FaFwdParams)
     p.num_stages, p.tile_cfg = plan.fwd_stages, plan.fwd_tile_cfg
     p.q, p.k, p.v, p.o = _fa_tensor(q), _fa_tensor(k), _fa_tensor(v), _fa_tensor(o)
     p.lse = lse.data_ptr()
@@ -225,16 +236,17 @@ def _run_bwd(plan: _Plan, q, k, v, o, lse, do) -> Tuple[torch.Tensor, torch.Tens
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
     lse = lse.to(torch.float32).contiguous()
-    p = L.FaBwdParams()
-    plan._fill(p)
+    p = plan.template(L.FaBwdParams)
     p.num_stages = plan.bwd_stages
     p.q, p.k, p.v, p.o, p.dout = _fa_tensor(q), _fa_tensor(k), _fa_tensor(v), _fa_tensor(o), _fa_tensor(do)
     p.dq, p.dk, p.dv = _fa_tensor(dq), _fa_tensor(dk), _fa_tensor(dv)
     p.lse = lse.data_ptr()
     lib = L.lib()
-    nbytes = C.c_size_t(0)
-    L.check(lib.fa_bwd_workspace_size(C.byref(p), C.byref(nbytes)))
-    ws = torch.empty(max(int(nbytes.value), 16), dtype=torch.uint8, device=q.device)
+    if plan._ws_bytes is None:  # a function of the shape alone
+        nbytes = C.c_size_t(0)
+        L.check(lib.fa_bwd_workspace_size(C.byref(p), C.byref(nbytes)))
+        plan._ws_bytes = max(int(nbytes.value), 16)
+    ws = torch.empty(plan._ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         L.check(lib.fa_bwd(C.byref(p), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(q.device).cuda_stream))
     return dq, dk, dv

@@ -86,13 +86,36 @@ def _default_pair_is_empty(mask_mod, q0: int, q1: int, k0: int, k1: int) -> bool
     return False
 
 
+_PLANS: dict = {}
+
+
+def _pair_plan(q, k, v, mask_mod, score_mod, q_offset: int, kv_offset: int, need_bwd: bool):
+    """The plan of one (q chunk, K/V chunk) pair, kept across ring steps and calls: a ring
+    revisits the same few geometries every step, and building a plan is host work on the
+    critical path of short chunks.  The key holds everything a plan depends on (shapes,
+    strides, 16-byte alignment, dtype, device, the mods, the offsets); the entry keeps the mod
+    objects alive so that their ids are not reused by others."""
+    from .flash_attn import _Plan
+
+    key = (tuple(q.shape), tuple(k.shape), q.stride(), k.stride(), v.stride(),
+           tuple(t.data_ptr() & 15 for t in (q, k, v)), q.dtype, q.device, id(mask_mod), id(score_mod),
+           q_offset, kv_offset, need_bwd)
+    hit = _PLANS.get(key)
+    if hit is not None and hit[1] is mask_mod and hit[2] is score_mod:
+        return hit[0]
+    if len(_PLANS) > 256:
+        _PLANS.clear()
+    plan = _Plan(q, k, v, mask_mod, score_mod, None, 64, 64, 0, None, need_bwd=need_bwd,
+                 offsets=(q_offset, kv_offset))
+    _PLANS[key] = (plan, mask_mod, score_mod)
+    return plan
+
+
 def gpu_partial_attention(q, k, v, mask_mod, score_mod, q_offset: int, kv_offset: int):
     """(o, lse) of q against one K/V chunk with global-position masks, on the tcgen05 kernel."""
-    from .flash_attn import _Plan, _run_fwd
+    from .flash_attn import _run_fwd
 
-    plan = _Plan(q, k, v, mask_mod, score_mod, None, 64, 64, 0, None, need_bwd=False,
-                 offsets=(q_offset, kv_offset))
-    return _run_fwd(plan, q, k, v)
+    return _run_fwd(_pair_plan(q, k, v, mask_mod, score_mod, q_offset, kv_offset, False), q, k, v)
 
 
 def gpu_merge(o_acc: torch.Tensor, lse_acc: torch.Tensor, o_part: torch.Tensor, lse_part: torch.Tensor) -> None:
@@ -180,11 +203,9 @@ def ring_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_m
 def gpu_partial_attention_bwd(q, k, v, o, lse, do, mask_mod, score_mod, q_offset: int, kv_offset: int):
     """(dq, dk, dv) contributions of one (q chunk, K/V chunk) pair, on the fused tcgen05
     backward: P is recomputed from the final logsumexp `lse` and delta from the final `o`."""
-    from .flash_attn import _Plan, _run_bwd
+    from .flash_attn import _run_bwd
 
-    plan = _Plan(q, k, v, mask_mod, score_mod, None, 64, 64, 0, None, need_bwd=True,
-                 offsets=(q_offset, kv_offset))
-    return _run_bwd(plan, q, k, v, o, lse, do)
+    return _run_bwd(_pair_plan(q, k, v, mask_mod, score_mod, q_offset, kv_offset, True), q, k, v, o, lse, do)
 
 
 def ring_attention_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, lse: torch.Tensor,
