@@ -257,9 +257,10 @@ def ring_attention_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
                 ks = slice(ki * Cl, (ki + 1) * Cl)
                 dq_c, dk_c, dv_c = attn_bwd_fn(q_p[qi], cur_k[:, :, ks], cur_v[:, :, ks], o_p[qi], l_p[qi], do_p[qi],
                                                mask_mod, score_mod, q0, k0)
-                dq_acc[:, :, qi * Cl:(qi + 1) * Cl] += dq_c.float()
-                dk_loc[:, :, ks] += dk_c.float()
-                dv_loc[:, :, ks] += dv_c.float()
+                # in-place adds cast the bf16 contributions inside the kernel (no fp32 temporaries)
+                dq_acc[:, :, qi * Cl:(qi + 1) * Cl].add_(dq_c)
+                dk_loc[:, :, ks].add_(dk_c)
+                dv_loc[:, :, ks].add_(dv_c)
                 if stats:
                     stats.pairs_computed += 1
         if world > 1:
